@@ -1,0 +1,139 @@
+// Shared device helpers for the sm_100a kernels: dtype conversion, 16-byte
+// packed accesses with cache hints, and fp32 reductions.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ako_b200.h"
+
+namespace ako_b200 {
+
+// ---------------------------------------------------------------- conversions
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+
+// N elements of T moved as one access (16 bytes when N * sizeof(T) == 16).
+template <typename T, int N>
+struct alignas(sizeof(T) * N) Packed {
+    T v[N];
+};
+
+// ------------------------------------------------------------ global accesses
+// Streaming loads: data read once per launch goes through the non-coherent
+// path and is not kept in L1 (inputs of these kernels are never written by
+// the same launch).
+template <typename T, int N>
+__device__ __forceinline__ Packed<T, N> ld_stream(const T* p) {
+    static_assert(sizeof(Packed<T, N>) == 16 || sizeof(Packed<T, N>) <= 8, "pack size");
+    Packed<T, N> r;
+    if constexpr (sizeof(Packed<T, N>) == 16) {
+        uint4 u;
+        asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                     : "l"(p));
+        *reinterpret_cast<uint4*>(&r) = u;
+    } else {
+        r = *reinterpret_cast<const Packed<T, N>*>(p);
+    }
+    return r;
+}
+
+// Plain cached load (weights and tables that every row or position re-reads).
+template <typename T, int N>
+__device__ __forceinline__ Packed<T, N> ld_cached(const T* p) {
+    return *reinterpret_cast<const Packed<T, N>*>(p);
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void st_global(T* p, const Packed<T, N>& v) {
+    *reinterpret_cast<Packed<T, N>*>(p) = v;
+}
+
+// Weight element `i` of a runtime-typed weight vector, as fp32.
+__device__ __forceinline__ float load_weight(const void* w, int wdtype, int64_t i) {
+    switch (wdtype) {
+        case AKO_B200_F16: return __half2float(static_cast<const __half*>(w)[i]);
+        case AKO_B200_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
+        default: return static_cast<const float*>(w)[i];
+    }
+}
+
+// N consecutive weights starting at element `i` (i * sizeof(W) is a multiple
+// of N * sizeof(W) rounded down to 16 bytes; the host checks the alignment).
+template <int N>
+__device__ __forceinline__ void load_weight_vec(const void* w, int wdtype, int64_t i, float (&out)[N]) {
+    if (wdtype == AKO_B200_F32) {
+        const float* p = static_cast<const float*>(w) + i;
+        if constexpr (N % 4 == 0) {
+#pragma unroll
+            for (int k = 0; k < N; k += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(p + k);
+                out[k] = q.x; out[k + 1] = q.y; out[k + 2] = q.z; out[k + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < N; ++k) out[k] = p[k];
+        }
+    } else if (wdtype == AKO_B200_BF16) {
+        const auto q = ld_cached<__nv_bfloat16, N>(static_cast<const __nv_bfloat16*>(w) + i);
+#pragma unroll
+        for (int k = 0; k < N; ++k) out[k] = __bfloat162float(q.v[k]);
+    } else {
+        const auto q = ld_cached<__half, N>(static_cast<const __half*>(w) + i);
+#pragma unroll
+        for (int k = 0; k < N; ++k) out[k] = __half2float(q.v[k]);
+    }
+}
+
+// ----------------------------------------------------------------- reductions
+// Butterfly over `WIDTH` lanes: every lane ends with the bitwise-identical sum
+// (fp32 addition is commutative, so partner pairs add the same two values).
+template <int WIDTH = 32>
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = WIDTH / 2; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off, WIDTH));
+    return v;
+}
+
+// In-place pairwise sum of N values (pairs at distance 1, 2, 4, ...).
+template <int N>
+__device__ __forceinline__ float tree_sum(float (&v)[N]) {
+#pragma unroll
+    for (int s = 1; s < N; s <<= 1) {
+#pragma unroll
+        for (int i = 0; i + s < N; i += 2 * s) v[i] = __fadd_rn(v[i], v[i + s]);
+    }
+    return v[0];
+}
+
+// Sum over a CTA of THREADS threads; every thread returns the same value
+// (warp partials are combined pairwise in a fixed order). `scratch` holds
+// THREADS/32 floats of shared memory and is used once per launch.
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+    v = warp_sum(v);
+    constexpr int WARPS = THREADS / 32;
+    if constexpr (WARPS == 1) {
+        return v;
+    } else {
+        if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float p[WARPS];
+#pragma unroll
+        for (int i = 0; i < WARPS; ++i) p[i] = scratch[i];
+        return tree_sum<WARPS>(p);
+    }
+}
+
+}  // namespace ako_b200

@@ -1,0 +1,155 @@
+// C-ABI entry points for RMSNorm and fused residual-add RMSNorm: argument
+// checks, choice of launch shape, dispatch on dtype.
+#include <climits>
+
+#include "rmsnorm.cuh"
+
+namespace ako_b200 {
+namespace {
+
+int g_override_tpr = 0;
+int g_override_nv = 0;
+
+// Launch shape for a row of `nvec` 16-byte vectors: the smallest row owner
+// (a warp, then CTAs of 64..1024 threads) whose registers hold the row with
+// four vectors per thread (eight for the widest rows).
+bool pick_shape(int64_t nvec, int* tpr, int* nv) {
+    if (g_override_tpr > 0 && static_cast<int64_t>(g_override_tpr) * g_override_nv >= nvec) {
+        *tpr = g_override_tpr;
+        *nv = g_override_nv;
+        return true;
+    }
+    struct Shape {
+        int tpr, nv;
+    };
+    static const Shape table[] = {{32, 1},  {32, 2},  {32, 4},   {64, 4},   {128, 4},
+                                  {256, 4}, {512, 4}, {1024, 4}, {1024, 8}};
+    for (const Shape& s : table) {
+        if (static_cast<int64_t>(s.tpr) * s.nv >= nvec) {
+            *tpr = s.tpr;
+            *nv = s.nv;
+            return true;
+        }
+    }
+    return false;
+}
+
+template <typename T, bool RES>
+int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
+    if (vector_ok) {
+        constexpr int VEC = 16 / sizeof(T);
+        int tpr = 0, nv = 0;
+        if (pick_shape(a.h / VEC, &tpr, &nv)) {
+            const int rc = launch_rms_rows<T, RES>(a, tpr, nv, st);
+            if (rc >= 0) return rc;
+        }
+    }
+    return launch_rms_generic<T, RES>(a, st);
+}
+
+template <bool RES>
+int dispatch(const RmsArgs& a, int dtype, bool vector_ok, cudaStream_t st) {
+    switch (dtype) {
+        case AKO_B200_F32: return run<float, RES>(a, vector_ok, st);
+        case AKO_B200_F16: return run<__half, RES>(a, vector_ok, st);
+        case AKO_B200_BF16: return run<__nv_bfloat16, RES>(a, vector_ok, st);
+        default: return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+    }
+}
+
+int check_common(const char* op, int64_t rows, int64_t h, int dtype, int wdtype) {
+    if (dtype_size(dtype) == 0)
+        return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype code %d", op, dtype);
+    if (dtype_size(wdtype) == 0)
+        return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "%s: unsupported weight dtype code %d", op, wdtype);
+    if (rows < 0) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: n_rows must be >= 0, got %lld", op,
+                                   static_cast<long long>(rows));
+    if (h < 1 || h > INT_MAX / 2)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: hidden_dim must be in [1, %d], got %lld", op,
+                         INT_MAX / 2, static_cast<long long>(h));
+    if (rows > INT_MAX)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: n_rows must be <= %d, got %lld", op, INT_MAX,
+                         static_cast<long long>(rows));
+    return AKO_B200_OK;
+}
+
+int check_operand(const char* op, const char* name, const void* p, int64_t stride, int64_t rows, int64_t h) {
+    if (p == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: %s is a null pointer", op, name);
+    if (rows > 1 && stride < h)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: %s row stride %lld is smaller than hidden_dim %lld", op,
+                         name, static_cast<long long>(stride), static_cast<long long>(h));
+    return AKO_B200_OK;
+}
+
+}  // namespace
+}  // namespace ako_b200
+
+using namespace ako_b200;
+
+extern "C" int ako_b200_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int weight_dtype, void* y,
+                                int64_t y_row_stride, int64_t n_rows, int64_t hidden_dim, double eps, int dtype,
+                                void* stream) {
+    clear_error();
+    const char* op = "ako_b200_rmsnorm";
+    int rc = check_common(op, n_rows, hidden_dim, dtype, weight_dtype);
+    if (rc) return rc;
+    if (n_rows == 0) return AKO_B200_OK;
+    if ((rc = check_operand(op, "x", x, x_row_stride, n_rows, hidden_dim))) return rc;
+    if ((rc = check_operand(op, "y", y, y_row_stride, n_rows, hidden_dim))) return rc;
+    if (weight == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: weight is a null pointer", op);
+
+    RmsArgs a{x, x_row_stride, nullptr, 0, weight, weight_dtype, y, y_row_stride, nullptr, 0,
+              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps)};
+    const int es = dtype_size(dtype);
+    const bool vector_ok = (hidden_dim * es) % 16 == 0 && aligned16(x) && aligned16(y) && aligned16(weight) &&
+                           stride_ok16(x_row_stride, n_rows, es) && stride_ok16(y_row_stride, n_rows, es);
+    return dispatch<false>(a, dtype, vector_ok, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride, const void* residual,
+                                         int64_t residual_row_stride, const void* weight, int weight_dtype, void* y,
+                                         int64_t y_row_stride, void* residual_out, int64_t residual_out_row_stride,
+                                         int64_t n_rows, int64_t hidden_dim, double eps, int dtype, void* stream) {
+    clear_error();
+    const char* op = "ako_b200_rmsnorm_residual";
+    int rc = check_common(op, n_rows, hidden_dim, dtype, weight_dtype);
+    if (rc) return rc;
+    if (n_rows == 0) return AKO_B200_OK;
+    if ((rc = check_operand(op, "x", x, x_row_stride, n_rows, hidden_dim))) return rc;
+    if ((rc = check_operand(op, "residual", residual, residual_row_stride, n_rows, hidden_dim))) return rc;
+    if ((rc = check_operand(op, "y", y, y_row_stride, n_rows, hidden_dim))) return rc;
+    if ((rc = check_operand(op, "residual_out", residual_out, residual_out_row_stride, n_rows, hidden_dim)))
+        return rc;
+    if (weight == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: weight is a null pointer", op);
+
+    RmsArgs a{x,      x_row_stride,  residual, residual_row_stride, weight, weight_dtype,
+              y,      y_row_stride,  residual_out, residual_out_row_stride,
+              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps)};
+    const int es = dtype_size(dtype);
+    const bool vector_ok = (hidden_dim * es) % 16 == 0 && aligned16(x) && aligned16(residual) && aligned16(y) &&
+                           aligned16(residual_out) && aligned16(weight) && stride_ok16(x_row_stride, n_rows, es) &&
+                           stride_ok16(residual_row_stride, n_rows, es) && stride_ok16(y_row_stride, n_rows, es) &&
+                           stride_ok16(residual_out_row_stride, n_rows, es);
+    return dispatch<true>(a, dtype, vector_ok, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ako_b200_rmsnorm_set_launch(int threads_per_row, int vectors_per_thread) {
+    clear_error();
+    if (threads_per_row == 0 && vectors_per_thread == 0) {
+        g_override_tpr = 0;
+        g_override_nv = 0;
+        return AKO_B200_OK;
+    }
+    static const int valid[][2] = {{32, 1},  {32, 2},  {32, 4},  {32, 8},  {64, 2},  {64, 4},   {64, 8},   {128, 1},
+                                   {128, 2}, {128, 4}, {128, 8}, {256, 1}, {256, 2}, {256, 4},  {256, 8},  {512, 1},
+                                   {512, 2}, {512, 4}, {512, 8}, {1024, 2}, {1024, 4}, {1024, 8}};
+    for (const auto& v : valid) {
+        if (v[0] == threads_per_row && v[1] == vectors_per_thread) {
+            g_override_tpr = threads_per_row;
+            g_override_nv = vectors_per_thread;
+            return AKO_B200_OK;
+        }
+    }
+    return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm launch shape (%d, %d) is not built", threads_per_row,
+                     vectors_per_thread);
+}

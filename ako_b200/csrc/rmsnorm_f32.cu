@@ -1,0 +1,7 @@
+// Instantiates the RMSNorm launchers for one storage dtype.
+#define AKO_RMS_INSTANTIATING
+#include "rmsnorm.cuh"
+
+namespace ako_b200 {
+AKO_RMS_DECLARE(float, )
+}  // namespace ako_b200

@@ -1,0 +1,159 @@
+/*
+ * ako_b200.h — C ABI of the B200 (sm_100a) kernels for AKO's memory-bound
+ * inference operators: RMSNorm, fused residual-add RMSNorm, RoPE and SwiGLU.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, a
+ * dtype code and a CUDA stream passed as `void*` (a `cudaStream_t`; NULL is
+ * the legacy default stream), launches asynchronously on that stream, never
+ * synchronizes and never allocates device memory. The return value is an
+ * `ako_b200_status`; on failure `ako_b200_last_error()` returns a message for
+ * the calling thread.
+ *
+ * Each function replaces one AKO kernel callable (a `KernelFn` in the
+ * reference's registry, reference file:line in the comment above it). A host
+ * wrapper with the reference's Python signature lives in
+ * `ako_b200/kernels.py`; it allocates the outputs with torch and calls these.
+ *
+ * Numerics follow the reference's PyTorch definitions: 16-bit inputs are
+ * upcast to fp32, every intermediate is an fp32 operation rounded to nearest
+ * in the reference's order (no fused multiply-add where the reference
+ * rounds between a multiply and an add), and the result is rounded once to
+ * the storage dtype.
+ */
+#ifndef AKO_B200_H_
+#define AKO_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of activations and outputs (and of the RMSNorm weight). */
+typedef enum {
+    AKO_B200_F32 = 0,
+    AKO_B200_F16 = 1,
+    AKO_B200_BF16 = 2
+} ako_b200_dtype;
+
+typedef enum {
+    AKO_B200_OK = 0,
+    AKO_B200_ERR_INVALID_ARGUMENT = 1, /* shape, stride, pointer or style problem  */
+    AKO_B200_ERR_UNSUPPORTED_DTYPE = 2, /* dtype code outside ako_b200_dtype        */
+    AKO_B200_ERR_CUDA = 3               /* the launch itself failed (cudaError_t)   */
+} ako_b200_status;
+
+/* RoPE pairing conventions (reference: ako/ops/rope_ref.py:1-11). */
+typedef enum {
+    AKO_B200_ROPE_NEOX = 0,        /* pairs (i, i + head_dim/2)  */
+    AKO_B200_ROPE_INTERLEAVED = 1  /* pairs (2i, 2i + 1)         */
+} ako_b200_rope_style;
+
+/* ABI version of this header; bumped on any signature change. */
+#define AKO_B200_ABI_VERSION 1
+
+int ako_b200_abi_version(void);
+
+/* Human-readable name of a status code (static storage). */
+const char* ako_b200_status_string(int status);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* ako_b200_last_error(void);
+
+/*
+ * RMSNorm over the last dimension:
+ *   y[m, :] = (x[m, :] * rsqrt(mean(x[m, :]^2) + eps)) * weight
+ * computed in fp32 and rounded once to `dtype`.
+ *
+ * Replaces the `rmsnorm` KernelFn `fn(x, weight, eps)`:
+ *   reference ako/ops/rmsnorm_ref.py:8-23 (definition),
+ *   ako/ops/rmsnorm_triton.py:139-160 (the GPU candidate it competes with),
+ *   ako/ops/rmsnorm.py:29-31 (call site).
+ *
+ * x, y:       n_rows rows of hidden_dim elements of `dtype`; row m starts at
+ *             element m * x_row_stride (y_row_stride); elements are contiguous.
+ * weight:     hidden_dim contiguous elements of `weight_dtype` (any of the
+ *             three dtypes).
+ * n_rows == 0 is a no-op. hidden_dim >= 1. Strides >= hidden_dim when
+ * n_rows > 1. Any alignment is accepted; 16-byte aligned rows use 128-bit
+ * accesses.
+ */
+int ako_b200_rmsnorm(const void* x, int64_t x_row_stride,
+                     const void* weight, int weight_dtype,
+                     void* y, int64_t y_row_stride,
+                     int64_t n_rows, int64_t hidden_dim,
+                     double eps, int dtype, void* stream);
+
+/*
+ * Fused residual add + RMSNorm:
+ *   residual_out = round_dtype(x + residual)
+ *   y            = rmsnorm(residual_out, weight, eps)
+ * Both outputs are written; inputs are read once.
+ *
+ * Replaces the `rmsnorm_residual` KernelFn `fn(x, residual, weight, eps)`
+ * returning `(normed, new_residual)`:
+ *   reference ako/ops/rmsnorm_ref.py:26-50 (definition),
+ *   ako/ops/rmsnorm_triton.py:163-192 (GPU candidate),
+ *   ako/ops/rmsnorm.py:54-56 (call site).
+ */
+int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride,
+                              const void* residual, int64_t residual_row_stride,
+                              const void* weight, int weight_dtype,
+                              void* y, int64_t y_row_stride,
+                              void* residual_out, int64_t residual_out_row_stride,
+                              int64_t n_rows, int64_t hidden_dim,
+                              double eps, int dtype, void* stream);
+
+/*
+ * Rotary position embedding on x of logical shape (batch, seq_len, n_heads,
+ * head_dim) with arbitrary element strides for the first three axes (the last
+ * axis is contiguous), so a (batch, n_heads, seq_len, head_dim)-contiguous
+ * tensor can be passed as its transposed view without a copy.
+ *   neox:        y[..., i]        = x[..., i] * c_i - x[..., i + D/2] * s_i
+ *                y[..., i + D/2]  = x[..., i] * s_i + x[..., i + D/2] * c_i
+ *   interleaved: the same on pairs (2i, 2i + 1).
+ * c_i = cos[s, i], s_i = sin[s, i]: fp32 tables of seq_len rows of head_dim/2
+ * contiguous values, row s at element s * table_row_stride (a row slice of a
+ * longer table is passed by pointer offset, no copy).
+ *
+ * Replaces the `rope` KernelFn `fn(x, cos, sin, style)`:
+ *   reference ako/ops/rope_ref.py:73-107 (definition), :57-70 (validation),
+ *   ako/ops/rope_triton.py:97-156 (GPU candidate),
+ *   ako/ops/rope.py:33-42 (call site).
+ */
+int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride_s, int64_t x_stride_h,
+                  const float* cos, const float* sin, int64_t table_row_stride,
+                  void* y, int64_t y_stride_b, int64_t y_stride_s, int64_t y_stride_h,
+                  int64_t batch, int64_t seq_len, int64_t n_heads, int64_t head_dim,
+                  int style, int dtype, void* stream);
+
+/*
+ * SwiGLU activation: y = silu(gate) * up = (gate / (1 + exp(-gate))) * up,
+ * evaluated in fp32 and rounded once. gate, up and y are n_rows x hidden_dim
+ * with independent row strides, so the packed layout (one [M, 2F] buffer whose
+ * halves are gate and up) is passed as two strided views without a copy.
+ *
+ * Replaces the `swiglu` KernelFn `fn(gate, up)`:
+ *   reference ako/ops/swiglu_ref.py:16-32 (definition),
+ *   ako/ops/swiglu_triton.py:55-81 (GPU candidate),
+ *   ako/ops/swiglu.py:22-24 (call site).
+ */
+int ako_b200_swiglu(const void* gate, int64_t gate_row_stride,
+                    const void* up, int64_t up_row_stride,
+                    void* y, int64_t y_row_stride,
+                    int64_t n_rows, int64_t hidden_dim,
+                    int dtype, void* stream);
+
+/*
+ * Launch-shape override for measurement sweeps: rows of `hidden_dim` use
+ * `threads_per_row` threads holding `vectors_per_thread` 16-byte vectors each.
+ * (0, 0) restores the built-in table. Not part of the reference's interface;
+ * it has no counterpart there. Process-wide, not thread-safe.
+ */
+int ako_b200_rmsnorm_set_launch(int threads_per_row, int vectors_per_thread);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AKO_B200_H_ */

@@ -1,0 +1,119 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the header
+declares, and rejects bad arguments with the documented status codes before
+touching the device. The KernelFn wrappers refuse CPU tensors (no fallback)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from ako_b200 import _native, kernels
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ako_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _native.LIB_PATH.exists():
+        from ako_b200.build import build
+
+        build()
+    return _native.lib()
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(ako_b200_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_bound_symbols() -> None:
+    assert declared_symbols() == sorted(_native.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib) -> None:
+    raw = ctypes.CDLL(str(_native.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+
+
+def test_abi_version(lib) -> None:
+    assert lib.ako_b200_abi_version() == _native.ABI_VERSION == 1
+
+
+def test_status_strings(lib) -> None:
+    assert lib.ako_b200_status_string(0) == b"AKO_B200_OK"
+    assert lib.ako_b200_status_string(3) == b"AKO_B200_ERR_CUDA"
+    assert lib.ako_b200_status_string(99) == b"AKO_B200_ERR_UNKNOWN"
+
+
+def test_rmsnorm_argument_errors(lib) -> None:
+    p = 16  # never dereferenced: every call below fails before a launch
+    assert lib.ako_b200_rmsnorm(p, 8, p, 0, p, 8, 4, 8, 1e-6, 7, None) == _native.ERR_UNSUPPORTED_DTYPE
+    assert b"dtype" in lib.ako_b200_last_error()
+    assert lib.ako_b200_rmsnorm(p, 8, p, 9, p, 8, 4, 8, 1e-6, 0, None) == _native.ERR_UNSUPPORTED_DTYPE
+    assert lib.ako_b200_rmsnorm(p, 8, p, 0, p, 8, -1, 8, 1e-6, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.ako_b200_rmsnorm(p, 8, p, 0, p, 8, 4, 0, 1e-6, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert b"hidden_dim" in lib.ako_b200_last_error()
+    assert lib.ako_b200_rmsnorm(None, 8, p, 0, p, 8, 4, 8, 1e-6, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert b"x is a null pointer" in lib.ako_b200_last_error()
+    assert lib.ako_b200_rmsnorm(p, 4, p, 0, p, 8, 4, 8, 1e-6, 0, None) == _native.ERR_INVALID_ARGUMENT
+    assert b"row stride" in lib.ako_b200_last_error()
+    # No rows: nothing to do, success without a launch.
+    assert lib.ako_b200_rmsnorm(None, 0, None, 0, None, 0, 0, 8, 1e-6, 2, None) == _native.OK
+    assert lib.ako_b200_last_error() == b""
+
+
+def test_residual_rope_swiglu_argument_errors(lib) -> None:
+    p = 16
+    assert lib.ako_b200_rmsnorm_residual(p, 8, None, 8, p, 0, p, 8, p, 8, 2, 8, 1e-5, 2, None) == 1
+    assert b"residual is a null pointer" in lib.ako_b200_last_error()
+    rope = lib.ako_b200_rope
+    assert rope(p, 0, 0, 0, p, p, 4, p, 0, 0, 0, 1, 1, 1, 8, 5, 2, None) == 1  # style
+    assert rope(p, 0, 0, 0, p, p, 4, p, 0, 0, 0, 1, 1, 1, 7, 0, 2, None) == 1  # odd head_dim
+    assert rope(p, 0, 0, 0, p, p, 4, p, 0, 0, 0, 1, 1, 1, 8, 0, 3, None) == 2  # dtype
+    assert rope(p, 0, 0, 0, p, p, 2, p, 0, 0, 0, 1, 2, 1, 8, 0, 2, None) == 1  # table stride < D/2
+    assert rope(None, 0, 0, 0, None, None, 0, None, 0, 0, 0, 0, 4, 2, 8, 0, 2, None) == 0  # empty batch
+    assert lib.ako_b200_swiglu(p, 8, p, 8, p, 8, 2, 8, 5, None) == 2
+    assert lib.ako_b200_swiglu(p, 4, p, 8, p, 8, 2, 8, 2, None) == 1
+    assert lib.ako_b200_swiglu(None, 0, None, 0, None, 0, 0, 8, 2, None) == 0
+
+
+def test_launch_override_validation(lib) -> None:
+    assert lib.ako_b200_rmsnorm_set_launch(128, 4) == 0
+    assert lib.ako_b200_rmsnorm_set_launch(0, 0) == 0
+    assert lib.ako_b200_rmsnorm_set_launch(96, 3) == 1
+
+
+@pytest.mark.parametrize(
+    "call",
+    [
+        lambda: kernels.rmsnorm_cuda_sm100(torch.randn(2, 8), torch.ones(8)),
+        lambda: kernels.rmsnorm_residual_cuda_sm100(torch.randn(2, 8), torch.randn(2, 8), torch.ones(8)),
+        lambda: kernels.rope_cuda_sm100(torch.randn(1, 2, 1, 8), torch.ones(2, 4), torch.zeros(2, 4)),
+        lambda: kernels.swiglu_cuda_sm100(torch.randn(2, 8), torch.randn(2, 8)),
+    ],
+    ids=["rmsnorm", "rmsnorm_residual", "rope", "swiglu"],
+)
+def test_wrappers_refuse_cpu_tensors(call) -> None:
+    with pytest.raises(ValueError, match="requires a CUDA tensor"):
+        call()
+
+
+def test_wrapper_shape_and_style_errors() -> None:
+    with pytest.raises(ValueError, match="Unknown RoPE style"):
+        kernels.rope_cuda_sm100(torch.randn(1, 2, 1, 8), torch.ones(2, 4), torch.zeros(2, 4), "bogus")
+    with pytest.raises(ValueError):
+        kernels.rmsnorm_residual_cuda_sm100(torch.randn(2, 8), torch.randn(2, 4), torch.ones(8))
+    with pytest.raises(ValueError):
+        kernels.swiglu_cuda_sm100(torch.randn(2, 8), torch.randn(2, 16))
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path) -> None:
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setenv("AKO_B200_LIB", str(tmp_path / "absent.so"))
+    with pytest.raises(_native.NativeLibraryError, match="not built"):
+        _native.lib()

@@ -1,0 +1,313 @@
+"""Parity of the sm_100a kernels with the reference, on a B200.
+
+Every call goes through the C ABI (``libako_b200.so``) via the KernelFn
+wrappers. Outputs are compared with the golden vectors the reference produced
+and with the CPU oracle on the same seeded inputs, under the gates of
+``helpers.assert_parity``: AKO's budget, AKO's ulp report (2 ulp for 16-bit,
+4 for fp32) and an elementwise ulp bound. The rounded residual and RoPE are
+compared bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import golden_data as gd
+from ako_b200 import _native, kernels
+from helpers import TORCH_DTYPE, assert_parity, normal, to_numpy, to_torch
+from oracle import ako_oracle as O
+from oracle import c_oracle as C
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = (O.F32, O.F16, O.BF16)
+
+
+def dev() -> torch.device:
+    return torch.device("cuda", 0)
+
+
+# ------------------------------------------------------------------ golden
+@pytest.mark.parametrize("case", gd.cases(), ids=[c["name"] for c in gd.cases()])
+def test_golden_vectors(cuda_device, case) -> None:
+    dt = case["dtype"]
+    t = lambda k: to_torch(gd.arr(case, k), dt if k not in ("cos", "sin") else O.F32, cuda_device)  # noqa: E731
+    op = case["op"]
+    if op == "rmsnorm":
+        out = {"y": kernels.rmsnorm_cuda_sm100(t("x"), t("w"), case["eps"])}
+    elif op == "rmsnorm_residual":
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(t("x"), t("r"), t("w"), case["eps"])
+        out = {"y": y, "ro": ro}
+    elif op == "rope":
+        out = {"y": kernels.rope_cuda_sm100(t("x"), t("cos"), t("sin"), case["style"])}
+    else:
+        out = {"y": kernels.swiglu_cuda_sm100(t("g"), t("u"))}
+    torch.cuda.synchronize()
+    if "ro" in out:
+        np.testing.assert_array_equal(to_numpy(out["ro"]), gd.arr(case, "ro"))
+    if op == "rope":
+        np.testing.assert_array_equal(to_numpy(out["y"]), gd.arr(case, "y"))
+    assert_parity(gd.arr(case, "y"), to_numpy(out["y"]), dt, op, case["name"])
+
+
+# ----------------------------------------------------------------- rmsnorm
+HIDDEN = (1, 2, 7, 64, 100, 256, 512, 1000, 1024, 2048, 4096, 5120, 8192, 8448, 11008, 16384, 32768, 65536)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("h", HIDDEN)
+def test_rmsnorm_widths(cuda_device, dtype: str, h: int) -> None:
+    rng = np.random.default_rng(h)
+    rows = 5 if h <= 16384 else 2
+    x = normal(rng, (rows, h), 0, 1, dtype)
+    r = normal(rng, (rows, h), 0, 1, dtype)
+    w = normal(rng, (h,), 1, 0.1, dtype)
+    y = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-6)
+    assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y), dtype, "rmsnorm", f"rmsnorm h={h}")
+    y, ro = kernels.rmsnorm_residual_cuda_sm100(
+        to_torch(x, dtype, cuda_device), to_torch(r, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-5
+    )
+    y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+    np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+    assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"residual h={h}")
+
+
+@pytest.mark.parametrize("rows", [1, 3, 4, 5, 127, 1000])
+def test_rmsnorm_row_counts(cuda_device, rows: int) -> None:
+    """Warp-per-row CTAs hold four rows; partial last CTAs must be exact."""
+    for h in (256, 1024, 4096):
+        rng = np.random.default_rng(rows * h)
+        x = normal(rng, (rows, h), 0, 1, O.BF16)
+        r = normal(rng, (rows, h), 0, 1, O.BF16)
+        w = normal(rng, (h,), 1, 0.1, O.BF16)
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(*(to_torch(a, O.BF16, cuda_device) for a in (x, r, w)), 1e-5)
+        y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, O.BF16)
+        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+        assert_parity(y_ref, to_numpy(y), O.BF16, "rmsnorm_residual", f"rows={rows} h={h}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rmsnorm_strided_and_misaligned_rows(cuda_device, dtype: str) -> None:
+    """Row-strided views run in place; unaligned ones take the scalar kernel."""
+    rng = np.random.default_rng(7)
+    base = to_torch(normal(rng, (6, 4100), 0, 1, dtype), dtype, cuda_device)
+    w = to_torch(normal(rng, (4096,), 1, 0.1, dtype), dtype, cuda_device)
+    for x in (base[:, :4096], base[:, 1:4097], base[:, 4:4100]):
+        y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+        ref = C.rmsnorm(to_numpy(x), to_numpy(w), 1e-6, dtype)
+        assert_parity(ref, to_numpy(y), dtype, "rmsnorm", "strided")
+
+
+@pytest.mark.parametrize("dtype", (O.F16, O.BF16))
+def test_rmsnorm_fp32_weight(cuda_device, dtype: str) -> None:
+    rng = np.random.default_rng(11)
+    x = normal(rng, (8, 4096), 0, 1, dtype)
+    w = normal(rng, (4096,), 1, 0.1, O.F32)
+    y = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, O.F32, cuda_device), 1e-6)
+    assert_parity(C.rmsnorm(x, w, 1e-6, dtype, O.F32), to_numpy(y), dtype, "rmsnorm", "fp32 weight")
+
+
+def test_every_rmsnorm_launch_shape(cuda_device) -> None:
+    """All built (threads per row, vectors per thread) shapes agree with the oracle."""
+    lib = _native.lib()
+    rng = np.random.default_rng(5)
+    shapes = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
+              (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
+              (1024, 2), (1024, 4), (1024, 8)]
+    try:
+        for dtype in (O.BF16, O.F32):
+            vec = 8 if dtype == O.BF16 else 4
+            for tpr, nv in shapes:
+                h = tpr * nv * vec - vec  # one vector short of full: exercises the column mask
+                if h < vec:
+                    continue
+                x = normal(rng, (9, h), 0, 1, dtype)
+                r = normal(rng, (9, h), 0, 1, dtype)
+                w = normal(rng, (h,), 1, 0.1, dtype)
+                assert lib.ako_b200_rmsnorm_set_launch(tpr, nv) == 0
+                y, ro = kernels.rmsnorm_residual_cuda_sm100(*(to_torch(a, dtype, cuda_device) for a in (x, r, w)), 1e-5)
+                y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+                np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+                assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"shape {tpr}x{nv} h={h}")
+    finally:
+        lib.ako_b200_rmsnorm_set_launch(0, 0)
+
+
+def test_rmsnorm_leading_dims_and_empty(cuda_device) -> None:
+    rng = np.random.default_rng(9)
+    x = normal(rng, (2, 3, 5, 512), 0, 1, O.BF16)
+    w = normal(rng, (512,), 1, 0.1, O.BF16)
+    y = kernels.rmsnorm_cuda_sm100(to_torch(x, O.BF16, cuda_device), to_torch(w, O.BF16, cuda_device))
+    assert y.shape == (2, 3, 5, 512)
+    assert_parity(C.rmsnorm(x, w, 1e-6, O.BF16), to_numpy(y), O.BF16, "rmsnorm", "4-d")
+    empty = torch.empty(0, 512, dtype=torch.bfloat16, device=cuda_device)
+    assert kernels.rmsnorm_cuda_sm100(empty, to_torch(w, O.BF16, cuda_device)).shape == (0, 512)
+
+
+def test_rmsnorm_rejects_oversized_hidden_dim(cuda_device) -> None:
+    x = torch.randn(1, kernels.MAX_HIDDEN_DIM + 2, device=cuda_device)
+    with pytest.raises(ValueError, match="hidden_dim"):
+        kernels.rmsnorm_residual_cuda_sm100(x, x, torch.ones(kernels.MAX_HIDDEN_DIM + 2, device=cuda_device))
+
+
+# -------------------------------------------------------------------- rope
+ROPE_SHAPES = [(2, 6, 3, 8), (1, 1, 32, 128), (8, 1, 8, 128), (2, 128, 8, 64), (1, 64, 32, 128),
+               (3, 17, 5, 128), (2, 9, 4, 256), (1, 5, 2, 6), (2, 4, 3, 2)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("style", O.ROPE_STYLES)
+@pytest.mark.parametrize("shape", ROPE_SHAPES, ids=[str(s) for s in ROPE_SHAPES])
+def test_rope_shapes(cuda_device, dtype: str, style: str, shape) -> None:
+    b, s, h, d = shape
+    rng = np.random.default_rng(b * 1000 + s * 10 + h)
+    x = normal(rng, shape, 0, 1, dtype)
+    cos, sin = O.build_rope_tables(s, d, offset=3)
+    y = kernels.rope_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(cos, O.F32, cuda_device),
+                                to_torch(sin, O.F32, cuda_device), style)
+    np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
+
+
+@pytest.mark.parametrize("dtype", (O.F16, O.BF16))
+def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str) -> None:
+    """q stored (B, H, S, D) and passed as .transpose(1, 2); decode-style
+    table slice cos[2047:2048] of an 8192-row table; neither is copied."""
+    rng = np.random.default_rng(21)
+    cos_full, sin_full = O.build_rope_tables(8192, 128)
+    cos_d, sin_d = to_torch(cos_full, O.F32, cuda_device), to_torch(sin_full, O.F32, cuda_device)
+    for b, hh, s, off in ((4, 32, 1, 2047), (2, 8, 33, 100)):
+        q_bhsd = normal(rng, (b, hh, s, 128), 0, 1, dtype)
+        q = to_torch(q_bhsd, dtype, cuda_device).transpose(1, 2)
+        y = kernels.rope_cuda_sm100(q, cos_d[off:off + s], sin_d[off:off + s], "neox")
+        assert y.stride() == q.stride()  # the output keeps the (B, H, S, D) layout
+        ref = O.rope(np.ascontiguousarray(q_bhsd.transpose(0, 2, 1, 3)), cos_full[off:off + s],
+                     sin_full[off:off + s], "neox", dtype)
+        np.testing.assert_array_equal(to_numpy(y), ref)
+
+
+def test_rope_position_zero_identity_and_empty(cuda_device) -> None:
+    x = torch.randn(2, 3, 4, 64, device=cuda_device, dtype=torch.bfloat16)
+    cos = torch.ones(3, 32, device=cuda_device)
+    sin = torch.zeros(3, 32, device=cuda_device)
+    assert torch.equal(kernels.rope_cuda_sm100(x, cos, sin), x)
+    e = torch.empty(0, 3, 4, 64, device=cuda_device, dtype=torch.bfloat16)
+    assert kernels.rope_cuda_sm100(e, cos, sin).shape == e.shape
+
+
+# ------------------------------------------------------------------ swiglu
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", [(1, 5632), (64, 11008), (7, 100), (3, 14336), (2, 3, 8448), (1, 1), (33, 24)])
+def test_swiglu_shapes(cuda_device, dtype: str, shape) -> None:
+    rng = np.random.default_rng(sum(shape))
+    g = normal(rng, shape, 0, 2, dtype)
+    u = normal(rng, shape, 0, 2, dtype)
+    y = kernels.swiglu_cuda_sm100(to_torch(g, dtype, cuda_device), to_torch(u, dtype, cuda_device))
+    assert y.shape == g.shape
+    assert_parity(C.swiglu(g, u, dtype), to_numpy(y), dtype, "swiglu", f"swiglu {shape}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_swiglu_packed_halves(cuda_device, dtype: str) -> None:
+    """One [M, 2F] projection output split into gate and up views, no copy."""
+    rng = np.random.default_rng(13)
+    for m, f in ((64, 5632), (1, 11008), (5, 100)):
+        packed = normal(rng, (m, 2 * f), 0, 2, dtype)
+        p = to_torch(packed, dtype, cuda_device)
+        y = kernels.swiglu_cuda_sm100(p[:, :f], p[:, f:])
+        ref = C.swiglu(np.ascontiguousarray(packed[:, :f]), np.ascontiguousarray(packed[:, f:]), dtype)
+        assert_parity(ref, to_numpy(y), dtype, "swiglu", f"packed {m}x{f}")
+
+
+def test_swiglu_extremes(cuda_device) -> None:
+    g = torch.tensor([[-100.0, -20.0, -1.0, 0.0, 1.0, 20.0, 100.0, float("inf")]], device=cuda_device)
+    u = torch.ones_like(g)
+    y = kernels.swiglu_cuda_sm100(g, u).cpu()
+    ref = C.swiglu(to_numpy(g), to_numpy(u), O.F32)
+    # expf of large arguments may differ by an ulp between CUDA and libm.
+    np.testing.assert_allclose(y.numpy()[:, :7], ref[:, :7], rtol=4 * 2.0**-23, atol=0)
+    assert torch.isinf(y[0, 7])
+
+
+# ------------------------------------------------------- launch semantics
+def test_runs_on_the_current_stream_and_in_a_graph(cuda_device) -> None:
+    x = torch.randn(64, 4096, device=cuda_device, dtype=torch.bfloat16)
+    r = torch.randn_like(x)
+    w = torch.randn(4096, device=cuda_device, dtype=torch.bfloat16)
+    eager_y, eager_ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gy, gro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+        gs = kernels.swiglu_cuda_sm100(x, r)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gy, eager_y) and torch.equal(gro, eager_ro)
+    assert torch.equal(gs, kernels.swiglu_cuda_sm100(x, r))
+
+
+def test_wrong_device_and_dtype_errors(cuda_device) -> None:
+    x = torch.randn(2, 64, device=cuda_device, dtype=torch.float64)
+    with pytest.raises(ValueError, match="float32/float16/bfloat16"):
+        kernels.rmsnorm_cuda_sm100(x, torch.ones(64, device=cuda_device, dtype=torch.float64))
+    with pytest.raises(ValueError, match="weight"):
+        kernels.rmsnorm_cuda_sm100(x.float(), torch.ones(64))
+
+
+# ------------------------------------------------- full BASELINE sizes
+def test_full_size_residual_against_torch_fp32(cuda_device) -> None:
+    """Config 2's largest cell (32768 x 16384 bf16): the rounded residual is
+    exact against torch's own add; the norm is within budget of an fp32 torch
+    evaluation of the reference formula; 64 sampled rows match the oracle."""
+    torch.manual_seed(0)
+    m, h = 32768, 16384
+    x = torch.randn(m, h, device=cuda_device, dtype=torch.bfloat16)
+    r = torch.randn(m, h, device=cuda_device, dtype=torch.bfloat16)
+    w = (torch.randn(h, device=cuda_device) * 0.1 + 1).to(torch.bfloat16)
+    y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+    assert torch.equal(ro, x + r)
+    for lo in range(0, m, 4096):  # the fp32 reference in slabs bounds the extra memory
+        rs = ro[lo:lo + 4096].float()
+        ref = (rs * torch.rsqrt(rs.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()).to(torch.bfloat16)
+        diff = (ref.float() - y[lo:lo + 4096].float()).abs().max().item()
+        assert diff <= 1e-5 + 1.6e-2 * ref.float().abs().max().item()
+    idx = torch.randint(0, m, (64,), device=cuda_device)
+    xs, rs_ = to_numpy(x[idx]), to_numpy(r[idx])
+    y_ref, ro_ref = C.rmsnorm_residual(xs, rs_, to_numpy(w), 1e-5, O.BF16)
+    np.testing.assert_array_equal(to_numpy(ro[idx]), ro_ref)
+    assert_parity(y_ref, to_numpy(y[idx]), O.BF16, "rmsnorm_residual", "full-size sample")
+
+
+def test_full_size_rope_and_swiglu_properties(cuda_device) -> None:
+    """Config 3's largest q (32 x 4096 x 32 x 128) and config 4's largest
+    swiglu (16384 x 14336), bf16: RoPE matches torch's fp32 evaluation of the
+    reference expression bit for bit; SwiGLU is within budget of torch's fp32
+    silu(g) * u, and zero wherever up is zero."""
+    torch.manual_seed(1)
+    b, s, hh, d = 32, 4096, 32, 128
+    q = torch.randn(b, s, hh, d, device=cuda_device, dtype=torch.bfloat16)
+    cos_np, sin_np = O.build_rope_tables(s, d)
+    cos, sin = to_torch(cos_np, O.F32, cuda_device), to_torch(sin_np, O.F32, cuda_device)
+    y = kernels.rope_cuda_sm100(q, cos, sin, "neox")
+    for lo in range(0, b, 4):
+        qc = q[lo:lo + 4].float()
+        x0, x1 = qc[..., :64], qc[..., 64:]
+        c, sn = cos[None, :, None, :], sin[None, :, None, :]
+        ref = torch.cat([x0 * c - x1 * sn, x0 * sn + x1 * c], dim=-1).to(torch.bfloat16)
+        assert torch.equal(ref, y[lo:lo + 4])
+    del q, y
+    g = torch.randn(16384, 14336, device=cuda_device, dtype=torch.bfloat16) * 2
+    u = torch.randn_like(g) * 2
+    u[::7] = 0
+    out = kernels.swiglu_cuda_sm100(g, u)
+    assert not out[::7].float().abs().max().item()
+    for lo in range(0, 16384, 2048):
+        ref = (torch.nn.functional.silu(g[lo:lo + 2048].float()) * u[lo:lo + 2048].float()).to(torch.bfloat16)
+        diff = (ref.float() - out[lo:lo + 2048].float()).abs().max().item()
+        assert diff <= 1e-5 + 1.6e-2 * ref.float().abs().max().item()
