@@ -42,10 +42,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr],
     ),
-    "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int]),
+    "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int, _c_int]),
+    "ako_b200_rope_set_launch": (_c_int, [_c_int]),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Status codes (ako_b200_status).
 OK = 0

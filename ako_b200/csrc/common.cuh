@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -96,6 +97,53 @@ __device__ __forceinline__ void load_weight_vec(const void* w, int wdtype, int64
     }
 }
 
+
+// ------------------------------------------------------------ paired access
+// Elements e and e + 1 of a pack as fp32, and back with one rounding each
+// (16-bit types convert two at a time: one cvt.rn.{bf16x2,f16x2}.f32).
+template <typename T, int N>
+__device__ __forceinline__ float2 get2(const Packed<T, N>& p, int e) {
+    if constexpr (std::is_same_v<T, float>) {
+        return make_float2(p.v[e], p.v[e + 1]);
+    } else if constexpr (std::is_same_v<T, __half>) {
+        return __half22float2(*reinterpret_cast<const __half2*>(&p.v[e]));
+    } else {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p.v[e]));
+    }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void put2(Packed<T, N>& p, int e, float a, float b) {
+    if constexpr (std::is_same_v<T, float>) {
+        p.v[e] = a;
+        p.v[e + 1] = b;
+    } else if constexpr (std::is_same_v<T, __half>) {
+        *reinterpret_cast<__half2*>(&p.v[e]) = __floats2half2_rn(a, b);
+    } else {
+        *reinterpret_cast<__nv_bfloat162*>(&p.v[e]) = __floats2bfloat162_rn(a, b);
+    }
+}
+
+// ----------------------------------------------------------- integer division
+// n / d for 32-bit unsigned n by a divisor fixed at launch, as a multiply-high
+// and a shift: Granlund & Montgomery, "Division by Invariant Integers using
+// Multiplication" (PLDI 1994), round-up variant with a 64-bit sum, exact for
+// every n < 2^32 and 1 <= d < 2^32.
+struct FastDiv {
+    uint32_t d, mul, shift;
+
+    __host__ static FastDiv make(uint32_t divisor) {
+        uint32_t l = 0;
+        while ((uint64_t(1) << l) < divisor) ++l;  // ceil(log2(d))
+        const uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - divisor)) / divisor + 1;
+        return FastDiv{divisor, static_cast<uint32_t>(m), l};
+    }
+
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, mul)) + n) >> shift);
+    }
+};
+
 // ----------------------------------------------------------------- reductions
 // Butterfly over `WIDTH` lanes: every lane ends with the bitwise-identical sum
 // (fp32 addition is commutative, so partner pairs add the same two values).
@@ -134,6 +182,39 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
         for (int i = 0; i < WARPS; ++i) p[i] = scratch[i];
         return tree_sum<WARPS>(p);
     }
+}
+
+
+// ------------------------------------------------------- thread-block clusters
+__device__ __forceinline__ unsigned cluster_ctarank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Full cluster barrier; orders this CTA's shared-memory writes before other
+// CTAs' reads that follow the barrier.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Reads a float at the same shared-memory offset as `p` in CTA `rank` of
+// this cluster (distributed shared memory).
+__device__ __forceinline__ float ld_dsmem_f32(const float* p, unsigned rank) {
+    const unsigned local = static_cast<unsigned>(__cvta_generic_to_shared(p));
+    unsigned remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
 }
 
 }  // namespace ako_b200

@@ -7,27 +7,41 @@
 namespace ako_b200 {
 namespace {
 
-int g_override_tpr = 0;
-int g_override_nv = 0;
+struct Shape {
+    int cluster, tpr, nv;
+};
 
-// Launch shape for a row of `nvec` 16-byte vectors: the smallest row owner
-// (a warp, then CTAs of 64..1024 threads) whose registers hold the row with
-// four vectors per thread (eight for the widest rows).
-bool pick_shape(int64_t nvec, int* tpr, int* nv) {
-    if (g_override_tpr > 0 && static_cast<int64_t>(g_override_tpr) * g_override_nv >= nvec) {
-        *tpr = g_override_tpr;
-        *nv = g_override_nv;
+Shape g_override = {0, 0, 0};
+
+// Launch shape for a row of `nvec` 16-byte vectors. Narrow rows go one per
+// warp; rows up to 512 vectors one per CTA with four vectors per thread;
+// wider rows are split over a cluster of 2, 4 or 8 such CTAs (each CTA keeps
+// a 512-vector slice, the width at which one CTA per row streams best), and
+// rows the cluster split cannot divide evenly fall back to one large CTA.
+bool pick_shape(int64_t nvec, Shape* out) {
+    const Shape& o = g_override;
+    if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
+        *out = o;
         return true;
     }
-    struct Shape {
-        int tpr, nv;
-    };
-    static const Shape table[] = {{32, 1},  {32, 2},  {32, 4},   {64, 4},   {128, 4},
-                                  {256, 4}, {512, 4}, {1024, 4}, {1024, 8}};
-    for (const Shape& s : table) {
+    static const Shape narrow[] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 4}, {1, 128, 4}};
+    for (const Shape& s : narrow) {
         if (static_cast<int64_t>(s.tpr) * s.nv >= nvec) {
-            *tpr = s.tpr;
-            *nv = s.nv;
+            *out = s;
+            return true;
+        }
+    }
+    struct Wide {
+        int64_t max_vec;
+        Shape split, single;
+    };
+    static const Wide wide[] = {{1024, {2, 128, 4}, {1, 256, 4}},
+                                {2048, {4, 128, 4}, {1, 512, 4}},
+                                {4096, {8, 128, 4}, {1, 1024, 4}},
+                                {8192, {8, 256, 4}, {1, 1024, 8}}};
+    for (const Wide& w : wide) {
+        if (nvec <= w.max_vec) {
+            *out = nvec % w.split.cluster == 0 ? w.split : w.single;
             return true;
         }
     }
@@ -38,9 +52,9 @@ template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok) {
         constexpr int VEC = 16 / sizeof(T);
-        int tpr = 0, nv = 0;
-        if (pick_shape(a.h / VEC, &tpr, &nv)) {
-            const int rc = launch_rms_rows<T, RES>(a, tpr, nv, st);
+        Shape s;
+        if (pick_shape(a.h / VEC, &s)) {
+            const int rc = launch_rms_rows<T, RES>(a, s.cluster, s.tpr, s.nv, st);
             if (rc >= 0) return rc;
         }
     }
@@ -133,23 +147,25 @@ extern "C" int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride, co
     return dispatch<true>(a, dtype, vector_ok, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int ako_b200_rmsnorm_set_launch(int threads_per_row, int vectors_per_thread) {
+extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_per_thread) {
     clear_error();
-    if (threads_per_row == 0 && vectors_per_thread == 0) {
-        g_override_tpr = 0;
-        g_override_nv = 0;
+    if (cluster == 0 && threads_per_row == 0 && vectors_per_thread == 0) {
+        g_override = {0, 0, 0};
         return AKO_B200_OK;
     }
-    static const int valid[][2] = {{32, 1},  {32, 2},  {32, 4},  {32, 8},  {64, 2},  {64, 4},   {64, 8},   {128, 1},
-                                   {128, 2}, {128, 4}, {128, 8}, {256, 1}, {256, 2}, {256, 4},  {256, 8},  {512, 1},
-                                   {512, 2}, {512, 4}, {512, 8}, {1024, 2}, {1024, 4}, {1024, 8}};
-    for (const auto& v : valid) {
-        if (v[0] == threads_per_row && v[1] == vectors_per_thread) {
-            g_override_tpr = threads_per_row;
-            g_override_nv = vectors_per_thread;
-            return AKO_B200_OK;
-        }
+    static const int single[][2] = {{32, 1},  {32, 2},  {32, 4},  {32, 8},  {64, 2},   {64, 4},   {64, 8},   {128, 1},
+                                    {128, 2}, {128, 4}, {128, 8}, {256, 1}, {256, 2},  {256, 4},  {256, 8},  {512, 1},
+                                    {512, 2}, {512, 4}, {512, 8}, {1024, 2}, {1024, 4}, {1024, 8}};
+    static const int split[][2] = {{64, 4}, {128, 2}, {128, 4}, {256, 4}, {512, 4}};
+    bool ok = false;
+    if (cluster == 1) {
+        for (const auto& v : single) ok |= v[0] == threads_per_row && v[1] == vectors_per_thread;
+    } else if (cluster == 2 || cluster == 4 || cluster == 8) {
+        for (const auto& v : split) ok |= v[0] == threads_per_row && v[1] == vectors_per_thread;
     }
-    return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm launch shape (%d, %d) is not built", threads_per_row,
-                     vectors_per_thread);
+    if (!ok)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm launch shape (cluster %d, %d threads, %d vectors) is not built",
+                         cluster, threads_per_row, vectors_per_thread);
+    g_override = {cluster, threads_per_row, vectors_per_thread};
+    return AKO_B200_OK;
 }

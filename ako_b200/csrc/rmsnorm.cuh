@@ -46,42 +46,51 @@ struct RmsShape {
     static constexpr int kRowsPerCta = kThreads / TPR;
 };
 
-template <typename T, int TPR, int NV, bool RES>
+// CLUSTER > 1: a row is split into CLUSTER equal slices, one per CTA of a
+// thread-block cluster; CTA partial sums are exchanged through distributed
+// shared memory, so each CTA holds only H / CLUSTER elements in registers.
+template <typename T, int TPR, int NV, bool RES, int CLUSTER>
 __global__ void __launch_bounds__(RmsShape<TPR>::kThreads)
 rms_rows_kernel(const RmsArgs a) {
     constexpr int VEC = 16 / sizeof(T);
     constexpr int THREADS = RmsShape<TPR>::kThreads;
     constexpr int ROWS = RmsShape<TPR>::kRowsPerCta;
+    static_assert(CLUSTER == 1 || ROWS == 1, "clusters split CTA-per-row shapes only");
     using P = Packed<T, VEC>;
     __shared__ float scratch[THREADS / 32 > 0 ? THREADS / 32 : 1];
+    __shared__ float cluster_part;
 
     const int lane = threadIdx.x % TPR;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * ROWS + threadIdx.x / TPR;
+    const int64_t row = CLUSTER > 1 ? static_cast<int64_t>(blockIdx.x / CLUSTER)
+                                    : static_cast<int64_t>(blockIdx.x) * ROWS + threadIdx.x / TPR;
     // Warp-per-row CTAs reduce with shuffles only, so a warp whose row is past
-    // the end can leave; CTA-per-row grids have exactly one CTA per row.
+    // the end can leave; CTA-per-row grids have exactly one CTA per row slice.
     if (ROWS > 1 && row >= a.rows) return;
+    // This CTA's slice of the row: columns [c0, c0 + width).
+    const int width = CLUSTER > 1 ? a.h / CLUSTER : a.h;
+    const int c0 = CLUSTER > 1 ? static_cast<int>(cluster_ctarank()) * width : 0;
 
-    const T* xr = static_cast<const T*>(a.x) + row * a.sx;
+    const T* xr = static_cast<const T*>(a.x) + row * a.sx + c0;
     P v[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
         const int col = (j * TPR + lane) * VEC;
-        if (col < a.h) v[j] = ld_stream<T, VEC>(xr + col);
+        if (col < width) v[j] = ld_stream<T, VEC>(xr + col);
     }
 
     if constexpr (RES) {
-        const T* rr = static_cast<const T*>(a.r) + row * a.sr;
-        T* ro = static_cast<T*>(a.ro) + row * a.sro;
+        const T* rr = static_cast<const T*>(a.r) + row * a.sr + c0;
+        T* ro = static_cast<T*>(a.ro) + row * a.sro + c0;
         P rv[NV];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const int col = (j * TPR + lane) * VEC;
-            if (col < a.h) rv[j] = ld_stream<T, VEC>(rr + col);
+            if (col < width) rv[j] = ld_stream<T, VEC>(rr + col);
         }
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const int col = (j * TPR + lane) * VEC;
-            if (col < a.h) {
+            if (col < width) {
 #pragma unroll
                 for (int e = 0; e < VEC; ++e)
                     v[j].v[e] = from_f32<T>(__fadd_rn(to_f32(v[j].v[e]), to_f32(rv[j].v[e])));
@@ -102,7 +111,7 @@ rms_rows_kernel(const RmsArgs a) {
             const float f = to_f32(v[j].v[e]);
             sq[e] = __fmul_rn(f, f);
         }
-        part[j] = col < a.h ? tree_sum<VEC>(sq) : 0.0f;
+        part[j] = col < width ? tree_sum<VEC>(sq) : 0.0f;
     }
     const float acc = tree_sum<NV>(part);
     float total;
@@ -111,14 +120,27 @@ rms_rows_kernel(const RmsArgs a) {
     } else {
         total = block_sum<THREADS>(acc, scratch);
     }
+    if constexpr (CLUSTER > 1) {
+        // Publish this slice's sum, then every CTA adds the CLUSTER partials
+        // pairwise in rank order (identical result in all CTAs). The second
+        // barrier is split: arrive now, wait before exit, so no CTA leaves
+        // while another may still read its shared memory.
+        if (threadIdx.x == 0) cluster_part = total;
+        cluster_sync_all();
+        float parts[CLUSTER];
+#pragma unroll
+        for (int r = 0; r < CLUSTER; ++r) parts[r] = ld_dsmem_f32(&cluster_part, r);
+        total = tree_sum<CLUSTER>(parts);
+        cluster_arrive();
+    }
     const float mean = __fdiv_rn(total, static_cast<float>(a.h));
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
 
-    T* yr = static_cast<T*>(a.y) + row * a.sy;
+    T* yr = static_cast<T*>(a.y) + row * a.sy + c0;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
         const int col = (j * TPR + lane) * VEC;
-        if (col < a.h) {
+        if (col < width) {
             float w[VEC];
             load_weight_vec<VEC>(a.w, a.wdtype, col, w);
             P o;
@@ -128,6 +150,7 @@ rms_rows_kernel(const RmsArgs a) {
             st_global<T, VEC>(yr + col, o);
         }
     }
+    if constexpr (CLUSTER > 1) cluster_wait();
 }
 
 constexpr int kGenericThreads = 256;
@@ -164,44 +187,86 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
     }
 }
 
-#define AKO_RMS_CASE(T, RES, TPR, NV)                                                               \
-    case TPR * 16 + NV: {                                                                           \
-        constexpr int rows_per_cta = RmsShape<TPR>::kRowsPerCta;                                    \
-        const int64_t grid = (a.rows + rows_per_cta - 1) / rows_per_cta;                            \
-        rms_rows_kernel<T, TPR, NV, RES><<<static_cast<unsigned>(grid), RmsShape<TPR>::kThreads, 0, \
-                                           st>>>(a);                                                \
-        return check_launch(RES ? "rmsnorm_residual" : "rmsnorm");                                  \
+// Launches `kernel` on `grid` CTAs of `threads`, grouped in clusters of
+// `cluster` CTAs along x when cluster > 1.
+template <typename Kernel>
+int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, const RmsArgs& a, cudaStream_t st,
+                       const char* name) {
+    if (grid > 0x7fffffff) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: too many rows", name);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (cluster > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(AKO_B200_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(err));
+    }
+    return check_launch(name);
+}
+
+#define AKO_RMS_CASE(T, RES, CL, TPR, NV)                                                     \
+    case (CL * 65536 + TPR * 16 + NV): {                                                          \
+        constexpr int rows_per_cta = RmsShape<TPR>::kRowsPerCta;                                 \
+        const int64_t grid = CL > 1 ? a.rows * CL : (a.rows + rows_per_cta - 1) / rows_per_cta;  \
+        return launch_rows_kernel(rms_rows_kernel<T, TPR, NV, RES, CL>, grid, RmsShape<TPR>::kThreads, \
+                                  CL, a, st, RES ? "rmsnorm_residual" : "rmsnorm");              \
     }
 
-#define AKO_RMS_ALL_CASES(T, RES)                                                                    \
-    AKO_RMS_CASE(T, RES, 32, 1)                                                                      \
-    AKO_RMS_CASE(T, RES, 32, 2)                                                                      \
-    AKO_RMS_CASE(T, RES, 32, 4)                                                                      \
-    AKO_RMS_CASE(T, RES, 32, 8)                                                                      \
-    AKO_RMS_CASE(T, RES, 64, 2)                                                                      \
-    AKO_RMS_CASE(T, RES, 64, 4)                                                                      \
-    AKO_RMS_CASE(T, RES, 64, 8)                                                                      \
-    AKO_RMS_CASE(T, RES, 128, 1)                                                                     \
-    AKO_RMS_CASE(T, RES, 128, 2)                                                                     \
-    AKO_RMS_CASE(T, RES, 128, 4)                                                                     \
-    AKO_RMS_CASE(T, RES, 128, 8)                                                                     \
-    AKO_RMS_CASE(T, RES, 256, 1)                                                                     \
-    AKO_RMS_CASE(T, RES, 256, 2)                                                                     \
-    AKO_RMS_CASE(T, RES, 256, 4)                                                                     \
-    AKO_RMS_CASE(T, RES, 256, 8)                                                                     \
-    AKO_RMS_CASE(T, RES, 512, 1)                                                                     \
-    AKO_RMS_CASE(T, RES, 512, 2)                                                                     \
-    AKO_RMS_CASE(T, RES, 512, 4)                                                                     \
-    AKO_RMS_CASE(T, RES, 512, 8)                                                                     \
-    AKO_RMS_CASE(T, RES, 1024, 2)                                                                    \
-    AKO_RMS_CASE(T, RES, 1024, 4)                                                                    \
-    AKO_RMS_CASE(T, RES, 1024, 8)
+#define AKO_RMS_ALL_CASES(T, RES) \
+    AKO_RMS_CASE(T, RES, 1, 32, 1) \
+    AKO_RMS_CASE(T, RES, 1, 32, 2) \
+    AKO_RMS_CASE(T, RES, 1, 32, 4) \
+    AKO_RMS_CASE(T, RES, 1, 32, 8) \
+    AKO_RMS_CASE(T, RES, 1, 64, 2) \
+    AKO_RMS_CASE(T, RES, 1, 64, 4) \
+    AKO_RMS_CASE(T, RES, 1, 64, 8) \
+    AKO_RMS_CASE(T, RES, 1, 128, 1) \
+    AKO_RMS_CASE(T, RES, 1, 128, 2) \
+    AKO_RMS_CASE(T, RES, 1, 128, 4) \
+    AKO_RMS_CASE(T, RES, 1, 128, 8) \
+    AKO_RMS_CASE(T, RES, 1, 256, 1) \
+    AKO_RMS_CASE(T, RES, 1, 256, 2) \
+    AKO_RMS_CASE(T, RES, 1, 256, 4) \
+    AKO_RMS_CASE(T, RES, 1, 256, 8) \
+    AKO_RMS_CASE(T, RES, 1, 512, 1) \
+    AKO_RMS_CASE(T, RES, 1, 512, 2) \
+    AKO_RMS_CASE(T, RES, 1, 512, 4) \
+    AKO_RMS_CASE(T, RES, 1, 512, 8) \
+    AKO_RMS_CASE(T, RES, 1, 1024, 2) \
+    AKO_RMS_CASE(T, RES, 1, 1024, 4) \
+    AKO_RMS_CASE(T, RES, 1, 1024, 8) \
+    AKO_RMS_CASE(T, RES, 2, 64, 4) \
+    AKO_RMS_CASE(T, RES, 2, 128, 2) \
+    AKO_RMS_CASE(T, RES, 2, 128, 4) \
+    AKO_RMS_CASE(T, RES, 2, 256, 4) \
+    AKO_RMS_CASE(T, RES, 2, 512, 4) \
+    AKO_RMS_CASE(T, RES, 4, 64, 4) \
+    AKO_RMS_CASE(T, RES, 4, 128, 2) \
+    AKO_RMS_CASE(T, RES, 4, 128, 4) \
+    AKO_RMS_CASE(T, RES, 4, 256, 4) \
+    AKO_RMS_CASE(T, RES, 4, 512, 4) \
+    AKO_RMS_CASE(T, RES, 8, 64, 4) \
+    AKO_RMS_CASE(T, RES, 8, 128, 2) \
+    AKO_RMS_CASE(T, RES, 8, 128, 4) \
+    AKO_RMS_CASE(T, RES, 8, 256, 4) \
+    AKO_RMS_CASE(T, RES, 8, 512, 4)
 
-// Launches the row-resident kernel for (tpr, nv); returns -1 when that pair
-// is not instantiated.
+// Launches the row-resident kernel for (cluster, tpr, nv); returns -1 when
+// that shape is not instantiated.
 template <typename T, bool RES>
-int launch_rms_rows(const RmsArgs& a, int tpr, int nv, cudaStream_t st) {
-    switch (tpr * 16 + nv) {
+int launch_rms_rows(const RmsArgs& a, int cluster, int tpr, int nv, cudaStream_t st) {
+    switch (cluster * 65536 + tpr * 16 + nv) {
         AKO_RMS_ALL_CASES(T, RES)
         default: return -1;
     }
@@ -215,8 +280,8 @@ int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
 
 // Instantiated once per dtype in rmsnorm_{f32,f16,bf16}.cu (compiled in parallel).
 #define AKO_RMS_DECLARE(T, KW)                                                        \
-    KW template int launch_rms_rows<T, false>(const RmsArgs&, int, int, cudaStream_t); \
-    KW template int launch_rms_rows<T, true>(const RmsArgs&, int, int, cudaStream_t);  \
+    KW template int launch_rms_rows<T, false>(const RmsArgs&, int, int, int, cudaStream_t); \
+    KW template int launch_rms_rows<T, true>(const RmsArgs&, int, int, int, cudaStream_t);  \
     KW template int launch_rms_generic<T, false>(const RmsArgs&, cudaStream_t);        \
     KW template int launch_rms_generic<T, true>(const RmsArgs&, cudaStream_t);
 

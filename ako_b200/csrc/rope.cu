@@ -32,11 +32,13 @@ struct RopeArgs {
     void* y;
     int64_t yb, ys, yh;
     int64_t n_pos;
-    int seq;
+    FastDiv seq;  // position -> (batch, seq) split
     int heads;
     int half;
     int chunks;  // chunks of NP pairs per head
 };
+
+int g_heads_per_thread = 0;  // 0: built-in choice
 
 template <int N>
 __device__ __forceinline__ void load_table(const float* p, float (&out)[N]) {
@@ -55,95 +57,107 @@ __device__ __forceinline__ void load_table(const float* p, float (&out)[N]) {
     }
 }
 
-// NP pairs per thread. VECTOR: the NP (neox) or 2*NP (interleaved) elements
-// of a chunk are one 16-byte access; otherwise elements are moved one by one.
-template <typename T, int NP, bool INTERLEAVED, bool VECTOR>
-__global__ void __launch_bounds__(1024) rope_kernel(const RopeArgs a) {
+__device__ __forceinline__ float rot_lo(float lo, float hi, float c, float s) {
+    return __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
+}
+__device__ __forceinline__ float rot_hi(float lo, float hi, float c, float s) {
+    return __fadd_rn(__fmul_rn(lo, s), __fmul_rn(hi, c));
+}
+
+// Vector path: thread (x = chunk, y = head group, z = position in the CTA)
+// owns NP consecutive pairs of HPT consecutive heads. Its NP cos/sin values
+// are loaded once; the 2 * HPT 16-byte loads of its heads are issued before
+// any arithmetic.
+template <typename T, int NP, bool INTERLEAVED, int HPT>
+__global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
+    constexpr int E = INTERLEAVED ? 2 * NP : NP;  // elements per 16-byte access
+    using P = Packed<T, E>;
     const int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.z + threadIdx.z;
     if (pos >= a.n_pos) return;
-    const int64_t b = pos / a.seq;
-    const int64_t s = pos - b * a.seq;
-    const float* crow = a.cos + s * a.ts;
-    const float* srow = a.sin + s * a.ts;
+    const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
+    const int64_t s = static_cast<int64_t>(static_cast<uint32_t>(pos) - b * a.seq.d);
+    const int c = threadIdx.x;  // blockDim.x == chunks
+    const int p0 = c * NP;
+    float cs[NP], sn[NP];
+    load_table<NP>(a.cos + s * a.ts + p0, cs);
+    load_table<NP>(a.sin + s * a.ts + p0, sn);
     const T* xpos = static_cast<const T*>(a.x) + b * a.xb + s * a.xs;
     T* ypos = static_cast<T*>(a.y) + b * a.yb + s * a.ys;
 
-    for (int c = threadIdx.x; c < a.chunks; c += blockDim.x) {
-        const int p0 = c * NP;  // first pair of the chunk
-        float cs[NP], sn[NP];
-        if constexpr (VECTOR) {
-            load_table<NP>(crow + p0, cs);
-            load_table<NP>(srow + p0, sn);
-        } else {
+    for (int h0 = threadIdx.y * HPT; h0 < a.heads; h0 += blockDim.y * HPT) {
+        P lo[HPT], hi[HPT];
 #pragma unroll
-            for (int k = 0; k < NP; ++k) { cs[k] = crow[p0 + k]; sn[k] = srow[p0 + k]; }
+        for (int j = 0; j < HPT; ++j) {
+            if (h0 + j < a.heads) {
+                const T* xp = xpos + (h0 + j) * a.xh;
+                if constexpr (INTERLEAVED) {
+                    lo[j] = ld_stream<T, E>(xp + 2 * p0);
+                } else {
+                    lo[j] = ld_stream<T, E>(xp + p0);
+                    hi[j] = ld_stream<T, E>(xp + a.half + p0);
+                }
+            }
         }
-
-        for (int h = threadIdx.y; h < a.heads; h += blockDim.y) {
-            const T* xp = xpos + h * a.xh;
-            T* yp = ypos + h * a.yh;
-            float lo[NP], hi[NP];
-            if constexpr (!INTERLEAVED) {
-                if constexpr (VECTOR) {
-                    const auto l = ld_stream<T, NP>(xp + p0);
-                    const auto u = ld_stream<T, NP>(xp + a.half + p0);
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) { lo[k] = to_f32(l.v[k]); hi[k] = to_f32(u.v[k]); }
+        for (int j = 0; j < HPT; ++j) {
+            if (h0 + j < a.heads) {
+                T* yp = ypos + (h0 + j) * a.yh;
+                if constexpr (INTERLEAVED) {
+                    P o;
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+                        const float2 v = get2<T, E>(lo[j], 2 * k);
+                        put2<T, E>(o, 2 * k, rot_lo(v.x, v.y, cs[k], sn[k]), rot_hi(v.x, v.y, cs[k], sn[k]));
+                    }
+                    st_global<T, E>(yp + 2 * p0, o);
                 } else {
+                    P ol, oh;
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) { lo[k] = to_f32(xp[p0 + k]); hi[k] = to_f32(xp[a.half + p0 + k]); }
-                }
-            } else {
-                if constexpr (VECTOR) {
-                    const auto q = ld_stream<T, 2 * NP>(xp + 2 * p0);
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { lo[k] = to_f32(q.v[2 * k]); hi[k] = to_f32(q.v[2 * k + 1]); }
-                } else {
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { lo[k] = to_f32(xp[2 * (p0 + k)]); hi[k] = to_f32(xp[2 * (p0 + k) + 1]); }
-                }
-            }
-
-            T olo[NP], ohi[NP];
-#pragma unroll
-            for (int k = 0; k < NP; ++k) {
-                olo[k] = from_f32<T>(__fsub_rn(__fmul_rn(lo[k], cs[k]), __fmul_rn(hi[k], sn[k])));
-                ohi[k] = from_f32<T>(__fadd_rn(__fmul_rn(lo[k], sn[k]), __fmul_rn(hi[k], cs[k])));
-            }
-
-            if constexpr (!INTERLEAVED) {
-                if constexpr (VECTOR) {
-                    Packed<T, NP> l, u;
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { l.v[k] = olo[k]; u.v[k] = ohi[k]; }
-                    st_global<T, NP>(yp + p0, l);
-                    st_global<T, NP>(yp + a.half + p0, u);
-                } else {
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { yp[p0 + k] = olo[k]; yp[a.half + p0 + k] = ohi[k]; }
-                }
-            } else {
-                if constexpr (VECTOR) {
-                    Packed<T, 2 * NP> q;
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { q.v[2 * k] = olo[k]; q.v[2 * k + 1] = ohi[k]; }
-                    st_global<T, 2 * NP>(yp + 2 * p0, q);
-                } else {
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) { yp[2 * (p0 + k)] = olo[k]; yp[2 * (p0 + k) + 1] = ohi[k]; }
+                    for (int k = 0; k < NP; k += 2) {
+                        const float2 l = get2<T, E>(lo[j], k);
+                        const float2 u = get2<T, E>(hi[j], k);
+                        put2<T, E>(ol, k, rot_lo(l.x, u.x, cs[k], sn[k]), rot_lo(l.y, u.y, cs[k + 1], sn[k + 1]));
+                        put2<T, E>(oh, k, rot_hi(l.x, u.x, cs[k], sn[k]), rot_hi(l.y, u.y, cs[k + 1], sn[k + 1]));
+                    }
+                    st_global<T, E>(yp + p0, ol);
+                    st_global<T, E>(yp + a.half + p0, oh);
                 }
             }
         }
     }
 }
 
-// Block shape: x = chunks of a head (<= 256), y = heads, z = positions, with
-// about 256 threads per CTA.
-dim3 rope_block(int chunks, int heads, int64_t n_pos) {
+// Any alignment and head_dim: one pair per thread, element accesses.
+template <typename T, bool INTERLEAVED>
+__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeArgs a) {
+    const int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.z + threadIdx.z;
+    if (pos >= a.n_pos) return;
+    const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
+    const int64_t s = static_cast<int64_t>(static_cast<uint32_t>(pos) - b * a.seq.d);
+    const T* xpos = static_cast<const T*>(a.x) + b * a.xb + s * a.xs;
+    T* ypos = static_cast<T*>(a.y) + b * a.yb + s * a.ys;
+    for (int p = threadIdx.x; p < a.half; p += blockDim.x) {
+        const float c = a.cos[s * a.ts + p];
+        const float sn = a.sin[s * a.ts + p];
+        const int il = INTERLEAVED ? 2 * p : p;
+        const int ih = INTERLEAVED ? 2 * p + 1 : a.half + p;
+        for (int h = threadIdx.y; h < a.heads; h += blockDim.y) {
+            const T* xp = xpos + h * a.xh;
+            T* yp = ypos + h * a.yh;
+            const float lo = to_f32(xp[il]), hi = to_f32(xp[ih]);
+            yp[il] = from_f32<T>(rot_lo(lo, hi, c, sn));
+            yp[ih] = from_f32<T>(rot_hi(lo, hi, c, sn));
+        }
+    }
+}
+
+// Block shape for `chunks` threads per head row: y covers heads in groups of
+// `hpt`, z packs positions so a CTA has about 256 threads.
+dim3 rope_block(int chunks, int head_groups, int64_t n_pos) {
     const int bx = chunks < 256 ? chunks : 256;
     int by = 256 / bx;
     if (by < 1) by = 1;
-    if (by > heads) by = heads;
+    if (by > head_groups) by = head_groups;
     int bz = 256 / (bx * by);
     if (bz < 1) bz = 1;
     if (bz > n_pos) bz = static_cast<int>(n_pos);
@@ -151,25 +165,42 @@ dim3 rope_block(int chunks, int heads, int64_t n_pos) {
     return dim3(bx, by, bz);
 }
 
-template <typename T, int NP, bool IL, bool VEC>
-int launch(RopeArgs a, cudaStream_t st) {
-    a.chunks = a.half / NP;
-    const dim3 block = rope_block(a.chunks, a.heads, a.n_pos);
+template <typename Kernel>
+int launch_rope(Kernel kernel, const RopeArgs& a, dim3 block, cudaStream_t st) {
     const int64_t grid = (a.n_pos + block.z - 1) / block.z;
     if (grid > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_rope: too many positions");
-    rope_kernel<T, NP, IL, VEC><<<static_cast<unsigned>(grid), block, 0, st>>>(a);
+    kernel<<<static_cast<unsigned>(grid), block, 0, st>>>(a);
     return check_launch("rope");
 }
 
-template <typename T>
-int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st) {
-    constexpr int VEC = 16 / sizeof(T);
-    if (!interleaved) {
-        if (vector_ok && a.half % VEC == 0) return launch<T, VEC, false, true>(a, st);
-        return launch<T, 1, false, false>(a, st);
+template <typename T, int NP, bool IL>
+int launch_vec(RopeArgs a, int hpt, cudaStream_t st) {
+    a.chunks = a.half / NP;
+    const int groups = (a.heads + hpt - 1) / hpt;
+    const dim3 block = rope_block(a.chunks, groups, a.n_pos);
+    switch (hpt) {
+        case 1: return launch_rope(rope_vec_kernel<T, NP, IL, 1>, a, block, st);
+        case 2: return launch_rope(rope_vec_kernel<T, NP, IL, 2>, a, block, st);
+        default: return launch_rope(rope_vec_kernel<T, NP, IL, 4>, a, block, st);
     }
-    if (vector_ok && a.half % (VEC / 2) == 0) return launch<T, VEC / 2, true, true>(a, st);
-    return launch<T, 1, true, false>(a, st);
+}
+
+template <typename T>
+int run(RopeArgs a, bool interleaved, bool vector_ok, cudaStream_t st) {
+    constexpr int VEC = 16 / sizeof(T);
+    // Heads per thread: several heads share a thread's table values and keep
+    // more loads in flight; one head per thread when there are few heads.
+    int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (a.heads >= 16 ? 2 : 1);
+    const int chunk_pairs = interleaved ? VEC / 2 : VEC;
+    // A CTA holds whole head rows (chunks <= 256 threads along x).
+    if (vector_ok && a.half % chunk_pairs == 0 && a.half / chunk_pairs <= 256) {
+        if (interleaved) return launch_vec<T, VEC / 2, true>(a, hpt, st);
+        return launch_vec<T, VEC, false>(a, hpt, st);
+    }
+    const int bx = a.half < 256 ? a.half : 256;
+    const dim3 block = rope_block(bx, a.heads, a.n_pos);
+    if (interleaved) return launch_rope(rope_scalar_kernel<T, true>, a, block, st);
+    return launch_rope(rope_scalar_kernel<T, false>, a, block, st);
 }
 
 }  // namespace
@@ -193,8 +224,8 @@ extern "C" int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride
     if (head_dim < 2 || head_dim % 2 != 0 || head_dim > INT_MAX / 2)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: head_dim must be even and >= 2, got %lld", op,
                          static_cast<long long>(head_dim));
-    if (seq_len > INT_MAX || n_heads > INT_MAX)
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: seq_len and n_heads must fit in int32", op);
+    if (seq_len > INT_MAX || n_heads > INT_MAX || batch > INT_MAX || batch * seq_len > static_cast<int64_t>(UINT32_MAX))
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: batch * seq_len must be < 2^32", op);
     if (batch == 0 || seq_len == 0 || n_heads == 0) return AKO_B200_OK;
     if (x == nullptr || y == nullptr || cos == nullptr || sin == nullptr)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null pointer", op);
@@ -209,8 +240,8 @@ extern "C" int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride
     if (seq_len == 1) x_stride_s = y_stride_s = table_row_stride = 0;
     if (n_heads == 1) x_stride_h = y_stride_h = 0;
 
-    RopeArgs a{x,  x_stride_b, x_stride_s, x_stride_h, cos, sin, table_row_stride, y, y_stride_b, y_stride_s,
-               y_stride_h, batch * seq_len, static_cast<int>(seq_len), static_cast<int>(n_heads),
+    RopeArgs a{x,          x_stride_b, x_stride_s, x_stride_h, cos, sin, table_row_stride, y, y_stride_b, y_stride_s,
+               y_stride_h, batch * seq_len, FastDiv::make(static_cast<uint32_t>(seq_len)), static_cast<int>(n_heads),
                static_cast<int>(half), 0};
     auto s16 = [&](int64_t st, int elem) { return ((st * elem) & 15) == 0; };
     const bool vector_ok = aligned16(x) && aligned16(y) && aligned16(cos) && aligned16(sin) &&
@@ -224,4 +255,13 @@ extern "C" int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride
         case AKO_B200_F16: return run<__half>(a, il, vector_ok, st);
         default: return run<__nv_bfloat16>(a, il, vector_ok, st);
     }
+}
+
+extern "C" int ako_b200_rope_set_launch(int heads_per_thread) {
+    clear_error();
+    if (heads_per_thread != 0 && heads_per_thread != 1 && heads_per_thread != 2 && heads_per_thread != 4)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rope heads per thread must be 0, 1, 2 or 4, got %d",
+                         heads_per_thread);
+    g_heads_per_thread = heads_per_thread;
+    return AKO_B200_OK;
 }

@@ -1,15 +1,24 @@
 // SwiGLU activation for sm_100a, plus its C-ABI entry point.
 //
 // Definition (reference ako/ops/swiglu_ref.py:16-32, F.silu on fp32):
-//   y = round_T( (g / (1 + exp(-g))) * u ),  g = float(gate), u = float(up)
-// with IEEE division and one fp32 rounding per operation, as torch's CPU silu
-// kernel evaluates it. expf is CUDA's (not the fast-math intrinsic).
+//   y = round_T( silu(g) * u ),  silu(g) = g / (1 + exp(-g)),
+//   g = float(gate), u = float(up).
+// fp32 outputs evaluate exactly that expression with CUDA's expf and IEEE
+// division, so they stay within a few fp32 ulp of the reference. 16-bit
+// outputs evaluate g * (1 / (1 + exp(-g))) * u with the MUFU exponential and
+// reciprocal (__expf, rcp.approx): the fp32 value is then within ~2.5e-6
+// relative of the reference's, three orders of magnitude below the spacing
+// of the stored bf16 (2^-8) or fp16 (2^-11) result, so the stored value is
+// the reference's or, rarely, its neighbour. That cuts the per-element work
+// from ~29 to ~10 instructions: the exact form is issue-bound on B200 at
+// HBM rate, the cheap one is not.
 //
 // Element-wise over an (n_rows x hidden_dim) matrix whose three operands have
 // independent row strides (the packed [M, 2F] layout is two strided views).
 // Work is a flat sequence of 16-byte vectors; a grid of a few CTAs per SM
 // strides over it, each thread keeping UNROLL vectors of both inputs in
-// flight before it computes.
+// flight before it computes. Row and column of a vector come from one
+// multiply-high division (FastDiv) when the operands are not dense.
 #include <climits>
 
 #include "common.cuh"
@@ -27,20 +36,32 @@ struct SwigluArgs {
     int64_t sy;
     int64_t total;  // vectors (or elements, scalar path) in the matrix
     int64_t per_row;
+    FastDiv row_div;  // divides by per_row (valid when total < 2^32)
 };
 
 constexpr int kThreads = 256;
 
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+template <typename T>
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    return __fmul_rn(s, u);
+    if constexpr (std::is_same_v<T, float>) {
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        return __fmul_rn(s, u);
+    } else {
+        return (g * rcp_approx(1.0f + __expf(-g))) * u;
+    }
 }
 
 // FLAT: all three operands are dense (row stride == hidden_dim), so vector
-// i sits at element i * VEC of each. Otherwise rows are recovered with a
-// 32-bit (NARROW) or 64-bit division.
+// i sits at element i * VEC of each. Otherwise rows come from FastDiv
+// (NARROW, total < 2^32) or a 64-bit division.
 template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW>
-__global__ void __launch_bounds__(kThreads) swiglu_kernel(const SwigluArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) swiglu_kernel(const SwigluArgs a) {
     using P = Packed<T, VEC>;
     const T* gp = static_cast<const T*>(a.g);
     const T* up = static_cast<const T*>(a.u);
@@ -60,9 +81,9 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const SwigluArgs a) {
                 } else {
                     int64_t row, col;
                     if constexpr (NARROW) {
-                        const uint32_t r32 = static_cast<uint32_t>(i) / static_cast<uint32_t>(a.per_row);
+                        const uint32_t r32 = a.row_div.div(static_cast<uint32_t>(i));
                         row = r32;
-                        col = static_cast<int64_t>(static_cast<uint32_t>(i) - r32 * static_cast<uint32_t>(a.per_row));
+                        col = static_cast<int64_t>(static_cast<uint32_t>(i) - r32 * a.row_div.d);
                     } else {
                         row = i / a.per_row;
                         col = i - row * a.per_row;
@@ -86,8 +107,16 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const SwigluArgs a) {
             const int64_t i = base + static_cast<int64_t>(k) * kThreads;
             if (i < a.total) {
                 P o;
+                if constexpr (VEC % 2 == 0) {
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) o.v[e] = from_f32<T>(silu_mul(to_f32(g[k].v[e]), to_f32(u[k].v[e])));
+                    for (int e = 0; e < VEC; e += 2) {
+                        const float2 gf = get2<T, VEC>(g[k], e);
+                        const float2 uf = get2<T, VEC>(u[k], e);
+                        put2<T, VEC>(o, e, silu_mul<T>(gf.x, uf.x), silu_mul<T>(gf.y, uf.y));
+                    }
+                } else {
+                    o.v[0] = from_f32<T>(silu_mul<T>(to_f32(g[k].v[0]), to_f32(u[k].v[0])));
+                }
                 st_global<T, VEC>(yp + yo[k], o);
             }
         }
@@ -95,7 +124,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const SwigluArgs a) {
 }
 
 template <typename T, int VEC, int UNROLL>
-int launch(const SwigluArgs& a, bool flat, cudaStream_t st) {
+int launch(SwigluArgs a, bool flat, cudaStream_t st) {
     const int64_t per_cta = static_cast<int64_t>(kThreads) * UNROLL;
     int64_t grid = (a.total + per_cta - 1) / per_cta;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 CTAs of 256 threads fill an SM
@@ -104,6 +133,7 @@ int launch(const SwigluArgs& a, bool flat, cudaStream_t st) {
     if (flat) {
         swiglu_kernel<T, VEC, UNROLL, true, true><<<g, kThreads, 0, st>>>(a);
     } else if (a.total <= static_cast<int64_t>(UINT_MAX)) {
+        a.row_div = FastDiv::make(static_cast<uint32_t>(a.per_row));
         swiglu_kernel<T, VEC, UNROLL, false, true><<<g, kThreads, 0, st>>>(a);
     } else {
         swiglu_kernel<T, VEC, UNROLL, false, false><<<g, kThreads, 0, st>>>(a);
@@ -120,7 +150,7 @@ int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaSt
         // Small problems (decode rows) spread over more CTAs; large ones keep
         // four vectors per thread in flight.
         if (a.total < static_cast<int64_t>(sm_count()) * kThreads * 4) return launch<T, VEC, 1>(a, flat, st);
-        return launch<T, VEC, 4>(a, flat, st);
+        return launch<T, VEC, 2>(a, flat, st);
     }
     a.per_row = h;
     a.total = rows * h;
@@ -153,7 +183,7 @@ extern "C" int ako_b200_swiglu(const void* gate, int64_t gate_row_stride, const 
     const bool vector_ok = (hidden_dim * es) % 16 == 0 && aligned16(gate) && aligned16(up) && aligned16(y) &&
                            stride_ok16(gate_row_stride, n_rows, es) && stride_ok16(up_row_stride, n_rows, es) &&
                            stride_ok16(y_row_stride, n_rows, es);
-    SwigluArgs a{gate, gate_row_stride, up, up_row_stride, y, y_row_stride, 0, 0};
+    SwigluArgs a{gate, gate_row_stride, up, up_row_stride, y, y_row_stride, 0, 0, FastDiv{1, 1, 0}};
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (dtype) {
         case AKO_B200_F32: return run<float>(a, n_rows, hidden_dim, vector_ok, flat, st);

@@ -61,6 +61,11 @@ WORKLOADS = {
     "swiglu_bf16_16384x14336": ("swiglu", (16384, 14336), torch.bfloat16),
     "swiglu_packed_bf16_16384x14336": ("swiglu_packed", (16384, 14336), torch.bfloat16),
     "swiglu_bf16_2048x14336": ("swiglu", (2048, 14336), torch.bfloat16),
+    "swiglu_packed_bf16_2048x14336": ("swiglu_packed", (2048, 14336), torch.bfloat16),
+    # small cases of the same kernels (a few hundred MB, above L2) for ncu captures
+    "rmsnorm_residual_bf16_2048x16384": ("rmsnorm_residual", (2048, 16384), torch.bfloat16),
+    "rmsnorm_residual_bf16_4096x4096": ("rmsnorm_residual", (4096, 4096), torch.bfloat16),
+    "rope_q_bf16_16x512x32x128": ("rope", (16, 512, 32, 128), torch.bfloat16),
 }
 DEFAULT_WORKLOAD = "rmsnorm_residual_bf16_32768x16384"
 OPS_EXTRA = [
@@ -198,10 +203,12 @@ def ncu_traffic(workload: str) -> int | None:
 
 # ---------------------------------------------------------------- extras
 def per_launch_us(fn, n: int, flush: torch.Tensor) -> list[float]:
-    """Device time of each launch, L2 flushed (2x its size written) before each."""
+    """Device time of each launch, L2 flushed before each by reading twice its
+    size (a read leaves clean lines, so the timed kernel pays no write-backs)."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    sink = torch.empty((), dtype=torch.int64, device=flush.device)
     for s, e in evs:
-        flush.zero_()
+        torch.sum(flush.view(torch.int64), dim=0, out=sink)
         s.record()
         fn()
         e.record()
@@ -218,9 +225,10 @@ def run_ops(device: torch.device, peak: float) -> dict:
             wl.step()
         us = per_launch_us(wl.step, 10, flush)
         mean_us = statistics.mean(us)
-        gbs = wl.bytes / (mean_us * 1e-6) / 1e9
+        med_us = statistics.median(us)
+        gbs = wl.bytes / (med_us * 1e-6) / 1e9
         out[name] = {"op": wl.op, **wl.desc, "dtype": str(wl.dtype).replace("torch.", ""),
-                     "bytes": wl.bytes, "us_mean": round(mean_us, 2), "us_median": round(statistics.median(us), 2),
+                     "bytes": wl.bytes, "us_mean": round(mean_us, 2), "us_median": round(med_us, 2),
                      "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
         del wl
         torch.cuda.empty_cache()

@@ -50,7 +50,7 @@ typedef enum {
 } ako_b200_rope_style;
 
 /* ABI version of this header; bumped on any signature change. */
-#define AKO_B200_ABI_VERSION 1
+#define AKO_B200_ABI_VERSION 2
 
 int ako_b200_abi_version(void);
 
@@ -145,12 +145,22 @@ int ako_b200_swiglu(const void* gate, int64_t gate_row_stride,
                     int dtype, void* stream);
 
 /*
- * Launch-shape override for measurement sweeps: rows of `hidden_dim` use
- * `threads_per_row` threads holding `vectors_per_thread` 16-byte vectors each.
- * (0, 0) restores the built-in table. Not part of the reference's interface;
- * it has no counterpart there. Process-wide, not thread-safe.
+ * Launch-shape override for measurement sweeps: rows are split over
+ * `cluster` CTAs (1, 2, 4 or 8; a thread-block cluster when > 1), each row
+ * slice held by `threads_per_row` threads with `vectors_per_thread` 16-byte
+ * vectors each. (0, 0, 0) restores the built-in table. A shape that cannot
+ * hold a given row is ignored for that row. Not part of the reference's
+ * interface; it has no counterpart there. Process-wide, not thread-safe.
  */
-int ako_b200_rmsnorm_set_launch(int threads_per_row, int vectors_per_thread);
+int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_per_thread);
+
+/*
+ * Launch-shape override for measurement sweeps: each RoPE thread rotates
+ * `heads_per_thread` heads (1, 2 or 4); 0 restores the built-in choice. Not
+ * part of the reference's interface; it has no counterpart there.
+ * Process-wide, not thread-safe.
+ */
+int ako_b200_rope_set_launch(int heads_per_thread);
 
 #ifdef __cplusplus
 }

@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol(lib) -> None:
 
 
 def test_abi_version(lib) -> None:
-    assert lib.ako_b200_abi_version() == _native.ABI_VERSION == 1
+    assert lib.ako_b200_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_status_strings(lib) -> None:
@@ -83,9 +83,12 @@ def test_residual_rope_swiglu_argument_errors(lib) -> None:
 
 
 def test_launch_override_validation(lib) -> None:
-    assert lib.ako_b200_rmsnorm_set_launch(128, 4) == 0
-    assert lib.ako_b200_rmsnorm_set_launch(0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_launch(96, 3) == 1
+    assert lib.ako_b200_rmsnorm_set_launch(1, 128, 4) == 0
+    assert lib.ako_b200_rmsnorm_set_launch(4, 128, 4) == 0
+    assert lib.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
+    assert lib.ako_b200_rmsnorm_set_launch(1, 96, 3) == 1
+    assert lib.ako_b200_rmsnorm_set_launch(3, 128, 4) == 1
+    assert lib.ako_b200_rmsnorm_set_launch(2, 1024, 8) == 1
 
 
 @pytest.mark.parametrize(
@@ -117,3 +120,34 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path) -> None:
     monkeypatch.setenv("AKO_B200_LIB", str(tmp_path / "absent.so"))
     with pytest.raises(_native.NativeLibraryError, match="not built"):
         _native.lib()
+
+
+def test_rope_launch_override_validation(lib) -> None:
+    assert lib.ako_b200_rope_set_launch(2) == 0
+    assert lib.ako_b200_rope_set_launch(0) == 0
+    assert lib.ako_b200_rope_set_launch(3) == 1
+
+
+def _fastdiv(d: int) -> tuple[int, int]:
+    """Host half of the kernels' FastDiv (csrc/common.cuh), restated."""
+    l = 0
+    while (1 << l) < d:
+        l += 1
+    m = ((1 << 32) * ((1 << l) - d)) // d + 1
+    assert 0 < m < (1 << 32)
+    return m, l
+
+
+@pytest.mark.parametrize("d", [1, 2, 3, 5, 7, 100, 704, 1376, 1792, 4095, 4096, 4097, 65535, 2**31 - 1, 2**31,
+                               2**31 + 1, 2**32 - 1])
+def test_multiply_high_division_is_exact(d: int) -> None:
+    """q = (mulhi(n, m) + n) >> l equals n // d over boundary and random n < 2^32."""
+    import random
+
+    m, l = _fastdiv(d)
+    rnd = random.Random(d)
+    ns = [0, 1, d - 1, d, d + 1, 2**32 - 1, 2**32 - d, (2**32 - 1) // d * d, (2**32 - 1) // d * d - 1]
+    ns += [rnd.randrange(2**32) for _ in range(2000)] + [k * d + r for k in (1, 7, 1000) for r in (0, d - 1)]
+    for n in ns:
+        if 0 <= n < 2**32:
+            assert ((((n * m) >> 32) + n) >> l) == n // d, (n, d)

@@ -110,29 +110,35 @@ def test_rmsnorm_fp32_weight(cuda_device, dtype: str) -> None:
 
 
 def test_every_rmsnorm_launch_shape(cuda_device) -> None:
-    """All built (threads per row, vectors per thread) shapes agree with the oracle."""
+    """All built (cluster, threads per row slice, vectors per thread) shapes
+    agree with the oracle, on rows one vector per CTA slice short of full."""
     lib = _native.lib()
     rng = np.random.default_rng(5)
-    shapes = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
+    single = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
               (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
               (1024, 2), (1024, 4), (1024, 8)]
+    split = [(64, 4), (128, 2), (128, 4), (256, 4), (512, 4)]
+    shapes = [(1, t, n) for t, n in single] + [(c, t, n) for c in (2, 4, 8) for t, n in split]
     try:
         for dtype in (O.BF16, O.F32):
             vec = 8 if dtype == O.BF16 else 4
-            for tpr, nv in shapes:
-                h = tpr * nv * vec - vec  # one vector short of full: exercises the column mask
-                if h < vec:
+            for cl, tpr, nv in shapes:
+                h = cl * (tpr * nv * vec - vec)  # each CTA slice one vector short: exercises the mask
+                if h < vec or h > 65536:
                     continue
-                x = normal(rng, (9, h), 0, 1, dtype)
-                r = normal(rng, (9, h), 0, 1, dtype)
+                rows = 9 if h <= 16384 else 3
+                x = normal(rng, (rows, h), 0, 1, dtype)
+                r = normal(rng, (rows, h), 0, 1, dtype)
                 w = normal(rng, (h,), 1, 0.1, dtype)
-                assert lib.ako_b200_rmsnorm_set_launch(tpr, nv) == 0
+                assert lib.ako_b200_rmsnorm_set_launch(cl, tpr, nv) == 0
                 y, ro = kernels.rmsnorm_residual_cuda_sm100(*(to_torch(a, dtype, cuda_device) for a in (x, r, w)), 1e-5)
                 y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
                 np.testing.assert_array_equal(to_numpy(ro), ro_ref)
-                assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"shape {tpr}x{nv} h={h}")
+                assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"shape {cl}x{tpr}x{nv} h={h}")
+                y1 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-6)
+                assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1), dtype, "rmsnorm", f"shape {cl}x{tpr}x{nv}")
     finally:
-        lib.ako_b200_rmsnorm_set_launch(0, 0)
+        lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
 
 
 def test_rmsnorm_leading_dims_and_empty(cuda_device) -> None:
@@ -185,6 +191,36 @@ def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str) -> N
         ref = O.rope(np.ascontiguousarray(q_bhsd.transpose(0, 2, 1, 3)), cos_full[off:off + s],
                      sin_full[off:off + s], "neox", dtype)
         np.testing.assert_array_equal(to_numpy(y), ref)
+
+
+@pytest.mark.parametrize("hpt", [1, 2, 4])
+@pytest.mark.parametrize("style", O.ROPE_STYLES)
+def test_rope_every_heads_per_thread(cuda_device, hpt: int, style: str) -> None:
+    """Each built heads-per-thread variant, head counts not divisible by it."""
+    lib = _native.lib()
+    rng = np.random.default_rng(hpt)
+    try:
+        assert lib.ako_b200_rope_set_launch(hpt) == 0
+        for dtype in DTYPES:
+            for b, s, hh, d in ((2, 7, 1, 128), (1, 3, 3, 64), (3, 5, 40, 128), (1, 9, 32, 128), (2, 2, 5, 16)):
+                x = normal(rng, (b, s, hh, d), 0, 1, dtype)
+                cos, sin = O.build_rope_tables(s, d, offset=11)
+                y = kernels.rope_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(cos, O.F32, cuda_device),
+                                            to_torch(sin, O.F32, cuda_device), style)
+                np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
+    finally:
+        lib.ako_b200_rope_set_launch(0)
+
+
+def test_rope_many_positions(cuda_device) -> None:
+    """batch * seq well past 2^16 positions exercises the position split."""
+    rng = np.random.default_rng(17)
+    b, s, hh, d = 37, 4099, 2, 32
+    x = normal(rng, (b, s, hh, d), 0, 1, O.BF16)
+    cos, sin = O.build_rope_tables(s, d)
+    y = kernels.rope_cuda_sm100(to_torch(x, O.BF16, cuda_device), to_torch(cos, O.F32, cuda_device),
+                                to_torch(sin, O.F32, cuda_device), "neox")
+    np.testing.assert_array_equal(to_numpy(y), C.rope(x, cos, sin, "neox", O.BF16))
 
 
 def test_rope_position_zero_identity_and_empty(cuda_device) -> None:
