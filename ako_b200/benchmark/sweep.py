@@ -1,0 +1,247 @@
+"""Per-cell sweep of BASELINE configs 1-4 on one GPU, with competitors.
+
+For every op / shape / dtype cell it reports the device time of the sm_100a
+kernel (median over launches, L2 flushed by a 2x-L2 read before each), the
+achieved GB/s on the algorithmic bytes, and the fraction of the measured HBM
+copy bandwidth. Competitors are timed the same way: the unfused reference
+(eager), its ``torch.compile`` form, ``F.rms_norm`` and, when the reference
+package is importable (``--reference-path``), AKO's own Triton kernels. Decode
+cells (one token per sequence) add the wall-clock latency per call of
+back-to-back calls, which is what a decode loop pays, and the replay time of
+a CUDA graph holding one call. Each cell is also checked against the eager
+reference with AKO's error budget.
+
+    python -m ako_b200.benchmark.sweep --out gpurun_out/sweep.json [--configs 1,2,3,4]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+import sys
+import time
+from pathlib import Path
+from typing import Any, Callable
+
+import torch
+
+from ako_b200 import kernels
+from ako_b200.dispatch import references as refs
+from ako_b200.dispatch.numerical import error_budget, error_in_ulps, max_abs_error_any
+
+L2_FLUSH_BYTES = 2 * 126 * 1024 * 1024
+DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
+
+
+def _reference_package(path: str | None):
+    if path and Path(path).exists() and path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        from ako.ops import rmsnorm_ref, rmsnorm_torch, rmsnorm_triton, rope_ref, rope_torch, rope_triton, swiglu_ref
+        from ako.ops import swiglu_torch, swiglu_triton
+    except ImportError:
+        return None
+    return {
+        "rmsnorm": {"eager": rmsnorm_ref.rmsnorm_ref, "compile": rmsnorm_torch.rmsnorm_compiled,
+                    "triton": rmsnorm_triton.rmsnorm_triton},
+        "rmsnorm_residual": {"eager": rmsnorm_ref.rmsnorm_residual_ref,
+                             "compile": rmsnorm_torch.rmsnorm_residual_compiled,
+                             "triton": rmsnorm_triton.rmsnorm_residual_triton},
+        "rope": {"eager": rope_ref.rope_ref, "compile": rope_torch.rope_compiled, "triton": rope_triton.rope_triton},
+        "swiglu": {"eager": swiglu_ref.swiglu_ref, "compile": swiglu_torch.swiglu_compiled,
+                   "triton": swiglu_triton.swiglu_triton},
+    }
+
+
+def _own_competitors():
+    return {
+        "rmsnorm": {"eager": refs.rmsnorm_ref, "compile": refs.rmsnorm_compiled},
+        "rmsnorm_residual": {"eager": refs.rmsnorm_residual_ref, "compile": refs.rmsnorm_residual_compiled},
+        "rope": {"eager": refs.rope_ref, "compile": refs.rope_compiled},
+        "swiglu": {"eager": refs.swiglu_ref, "compile": refs.swiglu_compiled},
+    }
+
+
+OURS = {
+    "rmsnorm": kernels.rmsnorm_cuda_sm100,
+    "rmsnorm_residual": kernels.rmsnorm_residual_cuda_sm100,
+    "rope": kernels.rope_cuda_sm100,
+    "swiglu": kernels.swiglu_cuda_sm100,
+}
+
+
+def cells(configs: set[int]) -> list[dict[str, Any]]:
+    out: list[dict[str, Any]] = []
+    if 1 in configs:
+        out.append({"config": 1, "op": "rmsnorm", "dtype": "fp32", "rows": 2048, "hidden": 4096, "eps": 1e-6})
+    if 2 in configs:
+        for dt in ("bf16", "fp16"):
+            for h in (2048, 4096, 8192, 16384):
+                for m in (1, 32, 512, 8192, 32768):
+                    out.append({"config": 2, "op": "rmsnorm_residual", "dtype": dt, "rows": m, "hidden": h,
+                                "eps": 1e-5, "decode": m <= 32})
+    if 3 in configs:
+        for dt in ("bf16", "fp16"):
+            for b in (1, 8, 32):
+                for s in (1, 512, 4096):
+                    for heads, which in ((32, "q"), (8, "k")):
+                        out.append({"config": 3, "op": "rope", "dtype": dt, "batch": b, "seq": s, "heads": heads,
+                                    "tensor": which, "head_dim": 128, "decode": s == 1})
+    if 4 in configs:
+        for dt in ("bf16", "fp16"):
+            for f in (5632, 11008, 14336):
+                for m in (1, 64, 2048, 16384):
+                    for packed in (False, True):
+                        out.append({"config": 4, "op": "swiglu", "dtype": dt, "rows": m, "hidden": f,
+                                    "packed": packed, "decode": m <= 64})
+    return out
+
+
+def make_inputs(cell: dict[str, Any], dev: torch.device, tables: dict) -> tuple[tuple, dict, int]:
+    """Seeded inputs, call kwargs and algorithmic bytes of one cell."""
+    dt = DTYPES[cell["dtype"]]
+    b = torch.tensor([], dtype=dt).element_size()
+    g = torch.Generator(device=dev).manual_seed(0)
+    rnd = lambda *s, m=0.0, sd=1.0: (torch.randn(*s, generator=g, device=dev) * sd + m).to(dt)  # noqa: E731
+    op = cell["op"]
+    if op in ("rmsnorm", "rmsnorm_residual"):
+        m, h = cell["rows"], cell["hidden"]
+        x, w = rnd(m, h), rnd(h, m=1.0, sd=0.1)
+        if op == "rmsnorm":
+            return (x, w, cell["eps"]), {}, 2 * m * h * b + h * b
+        return (x, rnd(m, h), w, cell["eps"]), {}, 4 * m * h * b + h * b
+    if op == "rope":
+        bb, s, hh, d = cell["batch"], cell["seq"], cell["heads"], cell["head_dim"]
+        cos_full, sin_full = tables[d]
+        off = 2047 if s == 1 else 0
+        x = rnd(bb, s, hh, d)
+        return (x, cos_full[off:off + s], sin_full[off:off + s], "neox"), {}, 2 * x.numel() * b + s * (d // 2) * 8
+    m, f = cell["rows"], cell["hidden"]
+    if cell["packed"]:
+        p = rnd(m, 2 * f, sd=2.0)
+        return (p[:, :f], p[:, f:]), {}, 3 * m * f * b
+    return (rnd(m, f, sd=2.0), rnd(m, f, sd=2.0)), {}, 3 * m * f * b
+
+
+def device_us(fn: Callable, args: tuple, n: int, flush: torch.Tensor) -> float:
+    sink = torch.empty((), dtype=torch.int64, device=flush.device)
+    for _ in range(3):
+        fn(*args)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for s, e in evs:
+        torch.sum(flush.view(torch.int64), dim=0, out=sink)
+        s.record()
+        fn(*args)
+        e.record()
+    torch.cuda.synchronize()
+    return statistics.median(s.elapsed_time(e) * 1e3 for s, e in evs)
+
+
+def wall_us(fn: Callable, args: tuple, batches: int = 15, inner: int = 50) -> float:
+    """Wall-clock per call of back-to-back calls (p50 over batches)."""
+    for _ in range(5):
+        fn(*args)
+    torch.cuda.synchronize()
+    samples = []
+    for _ in range(batches):
+        t0 = time.perf_counter()
+        for _ in range(inner):
+            fn(*args)
+        torch.cuda.synchronize()
+        samples.append((time.perf_counter() - t0) * 1e6 / inner)
+    return statistics.median(samples)
+
+
+def graph_us(fn: Callable, args: tuple, inner: int = 100) -> float | None:
+    """Device time per replay of a CUDA graph holding one call; None if capture fails."""
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn(*args)
+        torch.cuda.current_stream().wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn(*args)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(inner):
+            gr.replay()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) * 1e3 / inner
+    except Exception:  # noqa: BLE001 - a candidate that cannot be captured is reported as such
+        return None
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--configs", default="1,2,3,4")
+    ap.add_argument("--competitors", default="eager,compile,triton,native")
+    ap.add_argument("--reference-path", default="baseline/_ref")
+    ap.add_argument("--launches", type=int, default=15)
+    ap.add_argument("--peak-gbs", type=float, default=None)
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak = args.peak_gbs
+    if peak is None:
+        try:
+            peak = float(json.loads(Path("MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+        except (OSError, KeyError, ValueError):
+            peak = 6650.0
+    ref_pkg = _reference_package(args.reference_path)
+    comps = ref_pkg or _own_competitors()
+    wanted = set(args.competitors.split(","))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    tables = {128: refs.build_rope_tables(8192, 128, device=dev)}
+    results = []
+    for cell in cells({int(c) for c in args.configs.split(",")}):
+        inputs, kw, nbytes = make_inputs(cell, dev, tables)
+        op = cell["op"]
+        row: dict[str, Any] = {**cell, "bytes": nbytes}
+        ours = OURS[op]
+        out = ours(*inputs)
+        ref = comps[op]["eager"](*inputs)
+        row["max_error"] = max_abs_error_any(ref, out)
+        row["budget"] = error_budget(ref)
+        row["ulps"] = round(error_in_ulps(ref, out), 3)
+        row["parity"] = row["max_error"] <= row["budget"]
+        us = device_us(ours, inputs, args.launches, flush)
+        row["ours_us"] = round(us, 3)
+        row["ours_gbs"] = round(nbytes / us / 1e3, 1)
+        row["frac"] = round(nbytes / us / 1e3 / peak, 4)
+        candidates = {k: v for k, v in comps[op].items() if k in wanted}
+        if op == "rmsnorm" and "native" in wanted:
+            candidates["native"] = refs.rmsnorm_torch_native
+        for name, fn in candidates.items():
+            try:
+                row[f"{name}_us"] = round(device_us(fn, inputs, max(5, args.launches // 3), flush), 3)
+            except Exception as exc:  # noqa: BLE001 - a competitor that cannot run this cell
+                row[f"{name}_us"] = None
+                row[f"{name}_error"] = f"{type(exc).__name__}: {str(exc)[:120]}"
+        if cell.get("decode"):
+            row["ours_wall_us"] = round(wall_us(ours, inputs), 2)
+            row["ours_graph_us"] = graph_us(ours, inputs)
+            for name, fn in candidates.items():
+                if row.get(f"{name}_us") is not None:
+                    row[f"{name}_wall_us"] = round(wall_us(fn, inputs), 2)
+                    row[f"{name}_graph_us"] = graph_us(fn, inputs)
+        results.append(row)
+        print(json.dumps(row), flush=True)
+        del inputs, out, ref
+    summary = {"peak_gbs": peak, "reference_package": ref_pkg is not None,
+               "gpu": torch.cuda.get_device_name(dev), "cells": results}
+    if args.out:
+        Path(args.out).write_text(json.dumps(summary, indent=1))
+
+
+if __name__ == "__main__":
+    main()

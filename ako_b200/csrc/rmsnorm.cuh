@@ -142,7 +142,7 @@ rms_rows_kernel(const RmsArgs a) {
         const int col = (j * TPR + lane) * VEC;
         if (col < width) {
             float w[VEC];
-            load_weight_vec<VEC>(a.w, a.wdtype, col, w);
+            load_weight_vec<VEC>(a.w, a.wdtype, c0 + col, w);
             P o;
 #pragma unroll
             for (int e = 0; e < VEC; ++e)
