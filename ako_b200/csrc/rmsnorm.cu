@@ -13,37 +13,31 @@ struct Shape {
 
 Shape g_override = {0, 0, 0};
 
-// Launch shape for a row of `nvec` 16-byte vectors. Narrow rows go one per
-// warp; rows up to 512 vectors one per CTA with four vectors per thread;
-// wider rows are split over a cluster of 2, 4 or 8 such CTAs (each CTA keeps
-// a 512-vector slice, the width at which one CTA per row streams best), and
-// rows the cluster split cannot divide evenly fall back to one large CTA.
+// Launch shape for a row of `nvec` 16-byte vectors, from a sweep of every
+// built shape on B200 (bf16, fp16, fp32; 2048..16384 wide; 1 to 32768 rows).
+// One CTA per row with two vectors per thread streams best up to 512
+// threads (1024-vector rows): its registers stay low enough for several
+// CTAs per SM, so loads of the next rows are in flight while a row reduces.
+// Wider rows keep 512-1024 threads with 4 vectors each. Rows wider than one
+// CTA's registers hold (8192 vectors) are split over a cluster of 8 CTAs;
+// splitting narrower rows measured slower at every row count.
 bool pick_shape(int64_t nvec, Shape* out) {
     const Shape& o = g_override;
     if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
         *out = o;
         return true;
     }
-    static const Shape narrow[] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 4}, {1, 128, 4}};
-    for (const Shape& s : narrow) {
+    static const Shape table[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
+                                  {1, 256, 2}, {1, 512, 2}, {1, 512, 4}, {1, 1024, 4}};
+    for (const Shape& s : table) {
         if (static_cast<int64_t>(s.tpr) * s.nv >= nvec) {
             *out = s;
             return true;
         }
     }
-    struct Wide {
-        int64_t max_vec;
-        Shape split, single;
-    };
-    static const Wide wide[] = {{1024, {2, 128, 4}, {1, 256, 4}},
-                                {2048, {4, 128, 4}, {1, 512, 4}},
-                                {4096, {8, 128, 4}, {1, 1024, 4}},
-                                {8192, {8, 256, 4}, {1, 1024, 8}}};
-    for (const Wide& w : wide) {
-        if (nvec <= w.max_vec) {
-            *out = nvec % w.split.cluster == 0 ? w.split : w.single;
-            return true;
-        }
+    if (nvec <= 8192) {
+        *out = nvec % 8 == 0 ? Shape{8, 512, 2} : Shape{1, 1024, 8};
+        return true;
     }
     return false;
 }
@@ -153,10 +147,11 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
         g_override = {0, 0, 0};
         return AKO_B200_OK;
     }
-    static const int single[][2] = {{32, 1},  {32, 2},  {32, 4},  {32, 8},  {64, 2},   {64, 4},   {64, 8},   {128, 1},
-                                    {128, 2}, {128, 4}, {128, 8}, {256, 1}, {256, 2},  {256, 4},  {256, 8},  {512, 1},
-                                    {512, 2}, {512, 4}, {512, 8}, {1024, 2}, {1024, 4}, {1024, 8}};
-    static const int split[][2] = {{64, 4}, {128, 2}, {128, 4}, {256, 4}, {512, 4}};
+    static const int single[][2] = {{32, 1},  {32, 2},   {32, 4},   {32, 8},   {64, 2},   {64, 4},  {64, 8},  {128, 1},
+                                    {128, 2}, {128, 4},  {128, 8},  {256, 1},  {256, 2},  {256, 4}, {256, 8}, {512, 1},
+                                    {512, 2}, {512, 4},  {512, 8},  {1024, 1}, {1024, 2}, {1024, 4}, {1024, 8}};
+    static const int split[][2] = {{64, 4},  {128, 2}, {128, 4},  {256, 2}, {256, 4},
+                                   {512, 2}, {512, 4}, {1024, 1}, {1024, 2}};
     bool ok = false;
     if (cluster == 1) {
         for (const auto& v : single) ok |= v[0] == threads_per_row && v[1] == vectors_per_thread;

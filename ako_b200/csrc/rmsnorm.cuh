@@ -92,8 +92,11 @@ rms_rows_kernel(const RmsArgs a) {
             const int col = (j * TPR + lane) * VEC;
             if (col < width) {
 #pragma unroll
-                for (int e = 0; e < VEC; ++e)
-                    v[j].v[e] = from_f32<T>(__fadd_rn(to_f32(v[j].v[e]), to_f32(rv[j].v[e])));
+                for (int e = 0; e < VEC; e += 2) {
+                    const float2 xa = get2<T, VEC>(v[j], e);
+                    const float2 ra = get2<T, VEC>(rv[j], e);
+                    put2<T, VEC>(v[j], e, __fadd_rn(xa.x, ra.x), __fadd_rn(xa.y, ra.y));
+                }
                 st_global<T, VEC>(ro + col, v[j]);
             }
         }
@@ -107,9 +110,10 @@ rms_rows_kernel(const RmsArgs a) {
         const int col = (j * TPR + lane) * VEC;
         float sq[VEC];
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-            const float f = to_f32(v[j].v[e]);
-            sq[e] = __fmul_rn(f, f);
+        for (int e = 0; e < VEC; e += 2) {
+            const float2 f = get2<T, VEC>(v[j], e);
+            sq[e] = __fmul_rn(f.x, f.x);
+            sq[e + 1] = __fmul_rn(f.y, f.y);
         }
         part[j] = col < width ? tree_sum<VEC>(sq) : 0.0f;
     }
@@ -145,8 +149,10 @@ rms_rows_kernel(const RmsArgs a) {
             load_weight_vec<VEC>(a.w, a.wdtype, c0 + col, w);
             P o;
 #pragma unroll
-            for (int e = 0; e < VEC; ++e)
-                o.v[e] = from_f32<T>(__fmul_rn(__fmul_rn(to_f32(v[j].v[e]), inv), w[e]));
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 f = get2<T, VEC>(v[j], e);
+                put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w[e]), __fmul_rn(__fmul_rn(f.y, inv), w[e + 1]));
+            }
             st_global<T, VEC>(yr + col, o);
         }
     }
@@ -243,24 +249,37 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 512, 2) \
     AKO_RMS_CASE(T, RES, 1, 512, 4) \
     AKO_RMS_CASE(T, RES, 1, 512, 8) \
+    AKO_RMS_CASE(T, RES, 1, 1024, 1) \
     AKO_RMS_CASE(T, RES, 1, 1024, 2) \
     AKO_RMS_CASE(T, RES, 1, 1024, 4) \
     AKO_RMS_CASE(T, RES, 1, 1024, 8) \
     AKO_RMS_CASE(T, RES, 2, 64, 4) \
     AKO_RMS_CASE(T, RES, 2, 128, 2) \
     AKO_RMS_CASE(T, RES, 2, 128, 4) \
+    AKO_RMS_CASE(T, RES, 2, 256, 2) \
     AKO_RMS_CASE(T, RES, 2, 256, 4) \
+    AKO_RMS_CASE(T, RES, 2, 512, 2) \
     AKO_RMS_CASE(T, RES, 2, 512, 4) \
+    AKO_RMS_CASE(T, RES, 2, 1024, 1) \
+    AKO_RMS_CASE(T, RES, 2, 1024, 2) \
     AKO_RMS_CASE(T, RES, 4, 64, 4) \
     AKO_RMS_CASE(T, RES, 4, 128, 2) \
     AKO_RMS_CASE(T, RES, 4, 128, 4) \
+    AKO_RMS_CASE(T, RES, 4, 256, 2) \
     AKO_RMS_CASE(T, RES, 4, 256, 4) \
+    AKO_RMS_CASE(T, RES, 4, 512, 2) \
     AKO_RMS_CASE(T, RES, 4, 512, 4) \
+    AKO_RMS_CASE(T, RES, 4, 1024, 1) \
+    AKO_RMS_CASE(T, RES, 4, 1024, 2) \
     AKO_RMS_CASE(T, RES, 8, 64, 4) \
     AKO_RMS_CASE(T, RES, 8, 128, 2) \
     AKO_RMS_CASE(T, RES, 8, 128, 4) \
+    AKO_RMS_CASE(T, RES, 8, 256, 2) \
     AKO_RMS_CASE(T, RES, 8, 256, 4) \
-    AKO_RMS_CASE(T, RES, 8, 512, 4)
+    AKO_RMS_CASE(T, RES, 8, 512, 2) \
+    AKO_RMS_CASE(T, RES, 8, 512, 4) \
+    AKO_RMS_CASE(T, RES, 8, 1024, 1) \
+    AKO_RMS_CASE(T, RES, 8, 1024, 2)
 
 // Launches the row-resident kernel for (cluster, tpr, nv); returns -1 when
 // that shape is not instantiated.

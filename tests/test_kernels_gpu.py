@@ -116,8 +116,8 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
     rng = np.random.default_rng(5)
     single = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
               (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
-              (1024, 2), (1024, 4), (1024, 8)]
-    split = [(64, 4), (128, 2), (128, 4), (256, 4), (512, 4)]
+              (1024, 1), (1024, 2), (1024, 4), (1024, 8)]
+    split = [(64, 4), (128, 2), (128, 4), (256, 2), (256, 4), (512, 2), (512, 4), (1024, 1), (1024, 2)]
     shapes = [(1, t, n) for t, n in single] + [(c, t, n) for c in (2, 4, 8) for t, n in split]
     try:
         for dtype in (O.BF16, O.F32):
