@@ -12,6 +12,7 @@ from ako_b200.kernels import (
     rmsnorm_cuda_sm100,
     rmsnorm_residual_cuda_sm100,
     rope_cuda_sm100,
+    rope_qk_cuda_sm100,
     swiglu_cuda_sm100,
 )
 from ako_b200.plugin import register
@@ -29,6 +30,7 @@ __all__ = [
     "rope",
     "rope_cuda_sm100",
     "rope_qk",
+    "rope_qk_cuda_sm100",
     "swiglu",
     "swiglu_cuda_sm100",
 ]

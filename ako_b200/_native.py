@@ -38,6 +38,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64,
          _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_ptr],
     ),
+    "ako_b200_rope_qk": (
+        _c_int,
+        [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64,
+         _c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64,
+         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_ptr],
+    ),
     "ako_b200_swiglu": (
         _c_int,
         [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr],

@@ -34,6 +34,7 @@ def register_all(registry: KernelRegistry | None = None, *, force: bool = False)
         ("rmsnorm_residual", "rmsnorm_residual_ref", refs.rmsnorm_residual_ref, "pytorch", _PYTORCH_PRIORITY),
         ("rope", "rope_ref", refs.rope_ref, "pytorch", _PYTORCH_PRIORITY),
         ("swiglu", "swiglu_ref", refs.swiglu_ref, "pytorch", _PYTORCH_PRIORITY),
+        ("rope_qk", "rope_qk_ref", refs.rope_qk_ref, "pytorch", _PYTORCH_PRIORITY),
         ("rmsnorm", "rmsnorm_torch_native", refs.rmsnorm_torch_native, "torch_native", _BASELINE_PRIORITY),
     ]
     if refs.compile_enabled():
@@ -43,6 +44,7 @@ def register_all(registry: KernelRegistry | None = None, *, force: bool = False)
              _BASELINE_PRIORITY),
             ("rope", "rope_compiled", refs.rope_compiled, "torch_compile", _BASELINE_PRIORITY),
             ("swiglu", "swiglu_compiled", refs.swiglu_compiled, "torch_compile", _BASELINE_PRIORITY),
+            ("rope_qk", "rope_qk_compiled", refs.rope_qk_compiled, "torch_compile", _BASELINE_PRIORITY),
         ]
     for op, name, fn, backend, prio in entries:
         reg.register(KernelEntry(op, name, fn, backend, prio))
@@ -82,7 +84,18 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: str = "ne
 
 def rope_qk(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: str = "neox", *,
             kernel: str | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    return rope(q, cos, sin, style, kernel=kernel), rope(k, cos, sin, style, kernel=kernel)
+    """RoPE of a query/key pair, dispatched as one op (``rope_qk``).
+
+    The reference applies ``rope`` twice (``ako/ops/rope.py:45-58``); here the
+    pair is one dispatched op whose CUDA candidate is a single launch. A
+    ``kernel=`` naming a ``rope`` candidate keeps the reference's two calls.
+    """
+    register_all()
+    if kernel is not None and get_registry().get("rope", kernel) is not None:
+        return rope(q, cos, sin, style, kernel=kernel), rope(k, cos, sin, style, kernel=kernel)
+    fn = get_selector().select("rope_qk", q, k, cos, sin, forced=kernel, extra_key=style,
+                               call_kwargs={"style": style})
+    return fn(q, k, cos, sin, style)
 
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor, *, kernel: str | None = None) -> torch.Tensor:

@@ -1,4 +1,5 @@
-// Rotary position embedding for sm_100a, plus its C-ABI entry point.
+// Rotary position embedding for sm_100a, plus its C-ABI entry points
+// (ako_b200_rope for one tensor, ako_b200_rope_qk for a query/key pair).
 //
 // Definition (reference ako/ops/rope_ref.py:73-107):
 //   neox:        y_lo = x_lo * c - x_hi * s,  y_hi = x_lo * s + x_hi * c
@@ -8,13 +9,14 @@
 // reference's tensor expression, so the fp32 result is bit-identical to it
 // and only the final cast rounds.
 //
-// Work decomposition: one CTA slice per sequence position (b, s). A thread
-// owns a chunk of NP consecutive pairs of the head vector; it loads the NP
-// cos/sin values of that chunk once and applies them to every head it
-// visits, so the table is read once per position rather than once per head.
-// Threads in a warp cover consecutive chunks of consecutive heads, so every
-// 16-byte access of a warp falls into full 128-byte segments whatever the
-// head stride (the (B, H, S, D) layout passed as a transposed view included).
+// Work decomposition: a CTA slice per sequence position (b, s). A thread owns
+// a chunk of NP consecutive pairs of the head vector; it loads the NP cos/sin
+// values of that chunk once and applies them to every head it visits — the
+// heads of up to two tensors (q then k for rope_qk), so a q/k pair shares one
+// table read and one launch. Threads in a warp cover consecutive chunks of
+// consecutive heads, so every 16-byte access of a warp falls in full
+// 128-byte segments whatever the head stride (the (B, H, S, D) layout passed
+// as a transposed view included).
 #include <climits>
 
 #include "common.cuh"
@@ -23,19 +25,23 @@
 namespace ako_b200 {
 namespace {
 
-struct RopeArgs {
+// One rotated tensor: input and output views of logical shape (B, S, heads, D).
+struct RopeTensor {
     const void* x;
     int64_t xb, xs, xh;
+    void* y;
+    int64_t yb, ys, yh;
+    int heads;
+};
+
+struct RopeArgs {
+    RopeTensor t0, t1;  // heads [0, t0.heads) are t0's, the next t1.heads are t1's
     const float* cos;
     const float* sin;
     int64_t ts;
-    void* y;
-    int64_t yb, ys, yh;
     int64_t n_pos;
     FastDiv seq;  // position -> (batch, seq) split
-    int heads;
     int half;
-    int chunks;  // chunks of NP pairs per head
 };
 
 int g_heads_per_thread = 0;  // 0: built-in choice
@@ -64,10 +70,21 @@ __device__ __forceinline__ float rot_hi(float lo, float hi, float c, float s) {
     return __fadd_rn(__fmul_rn(lo, s), __fmul_rn(hi, c));
 }
 
+// Input and output row of head `h` (counted over both tensors) at (b, s).
+template <typename T>
+__device__ __forceinline__ void head_rows(const RopeArgs& a, int h, int64_t b, int64_t s, const T*& xp, T*& yp) {
+    const bool first = h < a.t0.heads;
+    const int64_t lh = first ? h : h - a.t0.heads;
+    const T* x = static_cast<const T*>(first ? a.t0.x : a.t1.x);
+    T* y = static_cast<T*>(first ? a.t0.y : a.t1.y);
+    xp = x + b * (first ? a.t0.xb : a.t1.xb) + s * (first ? a.t0.xs : a.t1.xs) + lh * (first ? a.t0.xh : a.t1.xh);
+    yp = y + b * (first ? a.t0.yb : a.t1.yb) + s * (first ? a.t0.ys : a.t1.ys) + lh * (first ? a.t0.yh : a.t1.yh);
+}
+
 // Vector path: thread (x = chunk, y = head group, z = position in the CTA)
 // owns NP consecutive pairs of HPT consecutive heads. Its NP cos/sin values
-// are loaded once; the 2 * HPT 16-byte loads of its heads are issued before
-// any arithmetic.
+// are loaded once; the 16-byte loads of all its heads are issued before any
+// arithmetic.
 template <typename T, int NP, bool INTERLEAVED, int HPT>
 __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
     constexpr int E = INTERLEAVED ? 2 * NP : NP;  // elements per 16-byte access
@@ -76,20 +93,20 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
     if (pos >= a.n_pos) return;
     const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
     const int64_t s = static_cast<int64_t>(static_cast<uint32_t>(pos) - b * a.seq.d);
-    const int c = threadIdx.x;  // blockDim.x == chunks
-    const int p0 = c * NP;
+    const int p0 = threadIdx.x * NP;  // blockDim.x == chunks per head
     float cs[NP], sn[NP];
     load_table<NP>(a.cos + s * a.ts + p0, cs);
     load_table<NP>(a.sin + s * a.ts + p0, sn);
-    const T* xpos = static_cast<const T*>(a.x) + b * a.xb + s * a.xs;
-    T* ypos = static_cast<T*>(a.y) + b * a.yb + s * a.ys;
+    const int heads = a.t0.heads + a.t1.heads;
 
-    for (int h0 = threadIdx.y * HPT; h0 < a.heads; h0 += blockDim.y * HPT) {
+    for (int h0 = threadIdx.y * HPT; h0 < heads; h0 += blockDim.y * HPT) {
         P lo[HPT], hi[HPT];
+        T* yrow[HPT];
 #pragma unroll
         for (int j = 0; j < HPT; ++j) {
-            if (h0 + j < a.heads) {
-                const T* xp = xpos + (h0 + j) * a.xh;
+            if (h0 + j < heads) {
+                const T* xp;
+                head_rows<T>(a, h0 + j, b, s, xp, yrow[j]);
                 if constexpr (INTERLEAVED) {
                     lo[j] = ld_stream<T, E>(xp + 2 * p0);
                 } else {
@@ -100,8 +117,8 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
         }
 #pragma unroll
         for (int j = 0; j < HPT; ++j) {
-            if (h0 + j < a.heads) {
-                T* yp = ypos + (h0 + j) * a.yh;
+            if (h0 + j < heads) {
+                T* yp = yrow[j];
                 if constexpr (INTERLEAVED) {
                     P o;
 #pragma unroll
@@ -134,16 +151,16 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeArgs a) {
     if (pos >= a.n_pos) return;
     const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
     const int64_t s = static_cast<int64_t>(static_cast<uint32_t>(pos) - b * a.seq.d);
-    const T* xpos = static_cast<const T*>(a.x) + b * a.xb + s * a.xs;
-    T* ypos = static_cast<T*>(a.y) + b * a.yb + s * a.ys;
+    const int heads = a.t0.heads + a.t1.heads;
     for (int p = threadIdx.x; p < a.half; p += blockDim.x) {
         const float c = a.cos[s * a.ts + p];
         const float sn = a.sin[s * a.ts + p];
         const int il = INTERLEAVED ? 2 * p : p;
         const int ih = INTERLEAVED ? 2 * p + 1 : a.half + p;
-        for (int h = threadIdx.y; h < a.heads; h += blockDim.y) {
-            const T* xp = xpos + h * a.xh;
-            T* yp = ypos + h * a.yh;
+        for (int h = threadIdx.y; h < heads; h += blockDim.y) {
+            const T* xp;
+            T* yp;
+            head_rows<T>(a, h, b, s, xp, yp);
             const float lo = to_f32(xp[il]), hi = to_f32(xp[ih]);
             yp[il] = from_f32<T>(rot_lo(lo, hi, c, sn));
             yp[ih] = from_f32<T>(rot_hi(lo, hi, c, sn));
@@ -151,8 +168,8 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeArgs a) {
     }
 }
 
-// Block shape for `chunks` threads per head row: y covers heads in groups of
-// `hpt`, z packs positions so a CTA has about 256 threads.
+// Block shape for `chunks` threads per head row: y covers head groups, z
+// packs positions so a CTA has about 256 threads.
 dim3 rope_block(int chunks, int head_groups, int64_t n_pos) {
     const int bx = chunks < 256 ? chunks : 256;
     int by = 256 / bx;
@@ -166,41 +183,102 @@ dim3 rope_block(int chunks, int head_groups, int64_t n_pos) {
 }
 
 template <typename Kernel>
-int launch_rope(Kernel kernel, const RopeArgs& a, dim3 block, cudaStream_t st) {
+int launch_rope(Kernel kernel, const RopeArgs& a, dim3 block, cudaStream_t st, const char* name) {
     const int64_t grid = (a.n_pos + block.z - 1) / block.z;
-    if (grid > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_rope: too many positions");
+    if (grid > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: too many positions", name);
     kernel<<<static_cast<unsigned>(grid), block, 0, st>>>(a);
-    return check_launch("rope");
+    return check_launch(name);
 }
 
 template <typename T, int NP, bool IL>
-int launch_vec(RopeArgs a, int hpt, cudaStream_t st) {
-    a.chunks = a.half / NP;
-    const int groups = (a.heads + hpt - 1) / hpt;
-    const dim3 block = rope_block(a.chunks, groups, a.n_pos);
+int launch_vec(const RopeArgs& a, int hpt, cudaStream_t st, const char* name) {
+    const int heads = a.t0.heads + a.t1.heads;
+    const dim3 block = rope_block(a.half / NP, (heads + hpt - 1) / hpt, a.n_pos);
     switch (hpt) {
-        case 1: return launch_rope(rope_vec_kernel<T, NP, IL, 1>, a, block, st);
-        case 2: return launch_rope(rope_vec_kernel<T, NP, IL, 2>, a, block, st);
-        default: return launch_rope(rope_vec_kernel<T, NP, IL, 4>, a, block, st);
+        case 1: return launch_rope(rope_vec_kernel<T, NP, IL, 1>, a, block, st, name);
+        case 2: return launch_rope(rope_vec_kernel<T, NP, IL, 2>, a, block, st, name);
+        default: return launch_rope(rope_vec_kernel<T, NP, IL, 4>, a, block, st, name);
     }
 }
 
 template <typename T>
-int run(RopeArgs a, bool interleaved, bool vector_ok, cudaStream_t st) {
+int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st, const char* name) {
     constexpr int VEC = 16 / sizeof(T);
-    // Heads per thread: several heads share a thread's table values and keep
-    // more loads in flight; one head per thread when there are few heads.
-    int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (a.heads >= 16 ? 2 : 1);
+    const int heads = a.t0.heads + a.t1.heads;
+    // Heads per thread: two heads share a thread's table values and keep
+    // more loads in flight (measured fastest for 8..40 heads at D = 128).
+    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (heads >= 8 ? 2 : 1);
     const int chunk_pairs = interleaved ? VEC / 2 : VEC;
-    // A CTA holds whole head rows (chunks <= 256 threads along x).
     if (vector_ok && a.half % chunk_pairs == 0 && a.half / chunk_pairs <= 256) {
-        if (interleaved) return launch_vec<T, VEC / 2, true>(a, hpt, st);
-        return launch_vec<T, VEC, false>(a, hpt, st);
+        if (interleaved) return launch_vec<T, VEC / 2, true>(a, hpt, st, name);
+        return launch_vec<T, VEC, false>(a, hpt, st, name);
     }
-    const int bx = a.half < 256 ? a.half : 256;
-    const dim3 block = rope_block(bx, a.heads, a.n_pos);
-    if (interleaved) return launch_rope(rope_scalar_kernel<T, true>, a, block, st);
-    return launch_rope(rope_scalar_kernel<T, false>, a, block, st);
+    const dim3 block = rope_block(a.half < 256 ? a.half : 256, heads, a.n_pos);
+    if (interleaved) return launch_rope(rope_scalar_kernel<T, true>, a, block, st, name);
+    return launch_rope(rope_scalar_kernel<T, false>, a, block, st, name);
+}
+
+struct RopeCall {
+    int64_t batch, seq, half;
+    int style, dtype;
+};
+
+// Checks shared by both entry points; fills the common part of `a`.
+int check_call(const char* op, const RopeCall& c, int64_t head_dim, const float* cos, const float* sin,
+               int64_t& table_row_stride) {
+    if (dtype_size(c.dtype) == 0)
+        return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype code %d", op, c.dtype);
+    if (c.style != AKO_B200_ROPE_NEOX && c.style != AKO_B200_ROPE_INTERLEAVED)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: unknown style code %d", op, c.style);
+    if (c.batch < 0 || c.seq < 0) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: negative size", op);
+    if (head_dim < 2 || head_dim % 2 != 0 || head_dim > INT_MAX / 2)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: head_dim must be even and >= 2, got %lld", op,
+                         static_cast<long long>(head_dim));
+    if (c.seq > INT_MAX || c.batch > INT_MAX || c.batch * c.seq > static_cast<int64_t>(UINT32_MAX))
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: batch * seq_len must be < 2^32", op);
+    if (c.batch == 0 || c.seq == 0) return AKO_B200_OK;  // nothing to rotate; no pointer is read
+    if (cos == nullptr || sin == nullptr)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null table pointer", op);
+    if (c.seq > 1 && table_row_stride < c.half)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: table row stride %lld is smaller than head_dim/2", op,
+                         static_cast<long long>(table_row_stride));
+    if (c.seq == 1) table_row_stride = 0;
+    return AKO_B200_OK;
+}
+
+// Builds one tensor's view; strides of extent-1 axes are zeroed so they
+// cannot defeat the 16-byte path. Returns false on a null pointer.
+bool make_tensor(RopeTensor& t, const void* x, int64_t xb, int64_t xs, int64_t xh, void* y, int64_t yb,
+                 int64_t ys, int64_t yh, int64_t heads, const RopeCall& c) {
+    if (heads > 0 && (x == nullptr || y == nullptr)) return false;
+    if (c.batch == 1) xb = yb = 0;
+    if (c.seq == 1) xs = ys = 0;
+    if (heads == 1) xh = yh = 0;
+    t = RopeTensor{x, xb, xs, xh, y, yb, ys, yh, static_cast<int>(heads)};
+    return true;
+}
+
+bool vector_ok(const RopeTensor& t, int es) {
+    if (t.heads == 0) return true;
+    auto s16 = [es](int64_t st) { return ((st * es) & 15) == 0; };
+    return aligned16(t.x) && aligned16(t.y) && s16(t.xb) && s16(t.xs) && s16(t.xh) && s16(t.yb) && s16(t.ys) &&
+           s16(t.yh);
+}
+
+int dispatch(RopeArgs& a, const RopeCall& c, void* stream, const char* name) {
+    const int es = dtype_size(c.dtype);
+    a.half = static_cast<int>(c.half);
+    a.n_pos = c.batch * c.seq;
+    a.seq = FastDiv::make(static_cast<uint32_t>(c.seq));
+    const bool vec = vector_ok(a.t0, es) && vector_ok(a.t1, es) && aligned16(a.cos) && aligned16(a.sin) &&
+                     ((a.ts * 4) & 15) == 0 && (c.half * es) % 16 == 0;
+    const bool il = c.style == AKO_B200_ROPE_INTERLEAVED;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (c.dtype) {
+        case AKO_B200_F32: return run<float>(a, il, vec, st, name);
+        case AKO_B200_F16: return run<__half>(a, il, vec, st, name);
+        default: return run<__nv_bfloat16>(a, il, vec, st, name);
+    }
 }
 
 }  // namespace
@@ -215,46 +293,46 @@ extern "C" int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride
                              void* stream) {
     clear_error();
     const char* op = "ako_b200_rope";
-    const int es = dtype_size(dtype);
-    if (es == 0) return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype code %d", op, dtype);
-    if (style != AKO_B200_ROPE_NEOX && style != AKO_B200_ROPE_INTERLEAVED)
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: unknown style code %d", op, style);
-    if (batch < 0 || seq_len < 0 || n_heads < 0)
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: negative size", op);
-    if (head_dim < 2 || head_dim % 2 != 0 || head_dim > INT_MAX / 2)
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: head_dim must be even and >= 2, got %lld", op,
-                         static_cast<long long>(head_dim));
-    if (seq_len > INT_MAX || n_heads > INT_MAX || batch > INT_MAX || batch * seq_len > static_cast<int64_t>(UINT32_MAX))
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: batch * seq_len must be < 2^32", op);
+    const RopeCall c{batch, seq_len, head_dim / 2, style, dtype};
+    int rc = check_call(op, c, head_dim, cos, sin, table_row_stride);
+    if (rc) return rc;
+    if (n_heads < 0 || n_heads > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: bad n_heads", op);
     if (batch == 0 || seq_len == 0 || n_heads == 0) return AKO_B200_OK;
-    if (x == nullptr || y == nullptr || cos == nullptr || sin == nullptr)
+    RopeArgs a{};
+    if (!make_tensor(a.t0, x, x_stride_b, x_stride_s, x_stride_h, y, y_stride_b, y_stride_s, y_stride_h, n_heads, c))
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null pointer", op);
-    const int64_t half = head_dim / 2;
-    if (seq_len > 1 && table_row_stride < half)
-        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: table row stride %lld is smaller than head_dim/2", op,
-                         static_cast<long long>(table_row_stride));
+    a.t1 = RopeTensor{nullptr, 0, 0, 0, nullptr, 0, 0, 0, 0};
+    a.cos = cos;
+    a.sin = sin;
+    a.ts = table_row_stride;
+    return dispatch(a, c, stream, "rope");
+}
 
-    // Strides of axes of extent 1 are never used; zero them so they do not
-    // defeat the 16-byte path.
-    if (batch == 1) x_stride_b = y_stride_b = 0;
-    if (seq_len == 1) x_stride_s = y_stride_s = table_row_stride = 0;
-    if (n_heads == 1) x_stride_h = y_stride_h = 0;
-
-    RopeArgs a{x,          x_stride_b, x_stride_s, x_stride_h, cos, sin, table_row_stride, y, y_stride_b, y_stride_s,
-               y_stride_h, batch * seq_len, FastDiv::make(static_cast<uint32_t>(seq_len)), static_cast<int>(n_heads),
-               static_cast<int>(half), 0};
-    auto s16 = [&](int64_t st, int elem) { return ((st * elem) & 15) == 0; };
-    const bool vector_ok = aligned16(x) && aligned16(y) && aligned16(cos) && aligned16(sin) &&
-                           s16(x_stride_b, es) && s16(x_stride_s, es) && s16(x_stride_h, es) &&
-                           s16(y_stride_b, es) && s16(y_stride_s, es) && s16(y_stride_h, es) &&
-                           s16(table_row_stride, 4) && (half * es) % 16 == 0;
-    const bool il = style == AKO_B200_ROPE_INTERLEAVED;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    switch (dtype) {
-        case AKO_B200_F32: return run<float>(a, il, vector_ok, st);
-        case AKO_B200_F16: return run<__half>(a, il, vector_ok, st);
-        default: return run<__nv_bfloat16>(a, il, vector_ok, st);
-    }
+extern "C" int ako_b200_rope_qk(const void* q, int64_t q_stride_b, int64_t q_stride_s, int64_t q_stride_h,
+                                const void* k, int64_t k_stride_b, int64_t k_stride_s, int64_t k_stride_h,
+                                const float* cos, const float* sin, int64_t table_row_stride, void* q_out,
+                                int64_t q_out_stride_b, int64_t q_out_stride_s, int64_t q_out_stride_h, void* k_out,
+                                int64_t k_out_stride_b, int64_t k_out_stride_s, int64_t k_out_stride_h,
+                                int64_t batch, int64_t seq_len, int64_t q_heads, int64_t k_heads, int64_t head_dim,
+                                int style, int dtype, void* stream) {
+    clear_error();
+    const char* op = "ako_b200_rope_qk";
+    const RopeCall c{batch, seq_len, head_dim / 2, style, dtype};
+    int rc = check_call(op, c, head_dim, cos, sin, table_row_stride);
+    if (rc) return rc;
+    if (q_heads < 0 || k_heads < 0 || q_heads + k_heads > INT_MAX)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: bad head counts", op);
+    if (batch == 0 || seq_len == 0 || q_heads + k_heads == 0) return AKO_B200_OK;
+    RopeArgs a{};
+    if (!make_tensor(a.t0, q, q_stride_b, q_stride_s, q_stride_h, q_out, q_out_stride_b, q_out_stride_s,
+                     q_out_stride_h, q_heads, c) ||
+        !make_tensor(a.t1, k, k_stride_b, k_stride_s, k_stride_h, k_out, k_out_stride_b, k_out_stride_s,
+                     k_out_stride_h, k_heads, c))
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null pointer", op);
+    a.cos = cos;
+    a.sin = sin;
+    a.ts = table_row_stride;
+    return dispatch(a, c, stream, "rope_qk");
 }
 
 extern "C" int ako_b200_rope_set_launch(int heads_per_thread) {

@@ -87,6 +87,12 @@ def rope_ref(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: str =
     return out.to(x.dtype)
 
 
+def rope_qk_ref(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                style: str = "neox") -> tuple[torch.Tensor, torch.Tensor]:
+    """``(rope_ref(q), rope_ref(k))``: the reference's query/key pair, two calls."""
+    return rope_ref(q, cos, sin, style), rope_ref(k, cos, sin, style)
+
+
 def swiglu_ref(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` in fp32 (fp64 stays fp64), cast back."""
     if gate.shape != up.shape:
@@ -123,6 +129,10 @@ def rmsnorm_residual_compiled(x, residual, weight, eps=1e-6):
 
 def rope_compiled(x, cos, sin, style="neox"):
     return _compiled_fn("rope", rope_ref)(x, cos, sin, style)
+
+
+def rope_qk_compiled(q, k, cos, sin, style="neox"):
+    return _compiled_fn("rope_qk", rope_qk_ref)(q, k, cos, sin, style)
 
 
 def swiglu_compiled(gate, up):

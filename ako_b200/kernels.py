@@ -176,30 +176,11 @@ def rope_cuda_sm100(
     if style not in ROPE_STYLES:
         raise ValueError(f"Unknown RoPE style '{style}', expected one of {ROPE_STYLES}")
     _require_cuda(x, fn)
-    if x.ndim != 4:
-        raise ValueError(f"Expected x of shape (batch, seq_len, n_heads, head_dim), got {tuple(x.shape)}")
-    batch, seq_len, n_heads, head_dim = x.shape
-    if head_dim % 2 != 0:
-        raise ValueError(f"head_dim must be even, got {head_dim}")
-    half = head_dim // 2
-    if cos.shape != sin.shape:
-        raise ValueError(f"cos/sin shape mismatch: {tuple(cos.shape)} vs {tuple(sin.shape)}")
-    if cos.shape != (seq_len, half):
-        raise ValueError(f"Expected cos/sin of shape {(seq_len, half)}, got {tuple(cos.shape)}")
-    if cos.device != x.device or sin.device != x.device:
-        raise ValueError(f"{fn}: cos/sin must be on {x.device}")
+    _check_rope_args(x, cos, sin, fn)
     code = _dtype_code(x, "x", fn)
-    if cos.dtype != torch.float32 or sin.dtype != torch.float32:
-        # The kernel reads fp32 tables; other table dtypes are converted the
-        # way the reference converts them (``cos.to(compute_dtype)``).
-        cos, sin = cos.to(torch.float32), sin.to(torch.float32)
-    if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
-        cos, sin = cos.contiguous(), sin.contiguous()
-    if x.stride(-1) != 1:
-        x = x.contiguous()
-    y = torch.empty_like(x)
-    if y.stride(-1) != 1:
-        y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    cos, sin = _rope_tables(cos, sin)
+    x, y = _rope_out(x)
+    batch, seq_len, n_heads, head_dim = x.shape
     with _DeviceGuard(x.device):
         status = _native.lib().ako_b200_rope(
             x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
@@ -209,6 +190,71 @@ def rope_cuda_sm100(
         )
     _native.raise_for_status(status, fn)
     return y
+
+
+def _check_rope_args(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, fn: str) -> None:
+    if x.ndim != 4:
+        raise ValueError(f"Expected x of shape (batch, seq_len, n_heads, head_dim), got {tuple(x.shape)}")
+    if x.shape[-1] % 2 != 0:
+        raise ValueError(f"head_dim must be even, got {x.shape[-1]}")
+    if cos.shape != sin.shape:
+        raise ValueError(f"cos/sin shape mismatch: {tuple(cos.shape)} vs {tuple(sin.shape)}")
+    if cos.shape != (x.shape[1], x.shape[-1] // 2):
+        raise ValueError(f"Expected cos/sin of shape {(x.shape[1], x.shape[-1] // 2)}, got {tuple(cos.shape)}")
+    if cos.device != x.device or sin.device != x.device:
+        raise ValueError(f"{fn}: cos/sin must be on {x.device}")
+
+
+def _rope_tables(cos: torch.Tensor, sin: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32:
+        cos, sin = cos.to(torch.float32), sin.to(torch.float32)
+    if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    return cos, sin
+
+
+def _rope_out(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    y = torch.empty_like(x)
+    if y.stride(-1) != 1:
+        y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    return x, y
+
+
+def rope_qk_cuda_sm100(
+    q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: str = "neox"
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """RoPE of a query/key pair in one launch; returns ``(rope(q), rope(k))``.
+
+    Same result as two ``rope_cuda_sm100`` calls (and as the reference's
+    ``rope_qk``, ``ako/ops/rope.py:45-58``), but each position's table values
+    are read once for the q and k heads together.
+    """
+    fn = "rope_qk_cuda_sm100"
+    if style not in ROPE_STYLES:
+        raise ValueError(f"Unknown RoPE style '{style}', expected one of {ROPE_STYLES}")
+    _require_cuda(q, fn)
+    _check_rope_args(q, cos, sin, fn)
+    _check_rope_args(k, cos, sin, fn)
+    if k.shape[:2] != q.shape[:2] or k.shape[-1] != q.shape[-1] or k.dtype != q.dtype or k.device != q.device:
+        raise ValueError(f"{fn}: q {tuple(q.shape)} and k {tuple(k.shape)} must share batch, seq_len, head_dim, dtype")
+    code = _dtype_code(q, "q", fn)
+    cos, sin = _rope_tables(cos, sin)
+    q, qo = _rope_out(q)
+    k, ko = _rope_out(k)
+    batch, seq_len, qh, d = q.shape
+    with _DeviceGuard(q.device):
+        status = _native.lib().ako_b200_rope_qk(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+            qo.data_ptr(), qo.stride(0), qo.stride(1), qo.stride(2),
+            ko.data_ptr(), ko.stride(0), ko.stride(1), ko.stride(2),
+            batch, seq_len, qh, k.shape[2], d, _STYLE_CODE[style], code, _stream(q.device),
+        )
+    _native.raise_for_status(status, fn)
+    return qo, ko
 
 
 def swiglu_cuda_sm100(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -248,4 +294,5 @@ CANDIDATES = (
     ("rmsnorm_residual", "rmsnorm_residual_cuda_sm100", rmsnorm_residual_cuda_sm100),
     ("rope", "rope_cuda_sm100", rope_cuda_sm100),
     ("swiglu", "swiglu_cuda_sm100", swiglu_cuda_sm100),
+    ("rope_qk", "rope_qk_cuda_sm100", rope_qk_cuda_sm100),
 )

@@ -128,6 +128,25 @@ int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride_s, int64_t
                   int style, int dtype, void* stream);
 
 /*
+ * RoPE of a query/key pair in one launch: q (batch, seq_len, q_heads,
+ * head_dim) and k (batch, seq_len, k_heads, head_dim), each with its own
+ * strides, rotated with the same table; each position's cos/sin values are
+ * read once for all q_heads + k_heads heads. Same arithmetic as
+ * ako_b200_rope, so each output equals what ako_b200_rope gives for that
+ * tensor.
+ *
+ * Replaces the reference's pair of rope calls in `rope_qk`
+ * (ako/ops/rope.py:45-58; decoder call site ako/models/decoder.py:174-175).
+ */
+int ako_b200_rope_qk(const void* q, int64_t q_stride_b, int64_t q_stride_s, int64_t q_stride_h,
+                     const void* k, int64_t k_stride_b, int64_t k_stride_s, int64_t k_stride_h,
+                     const float* cos, const float* sin, int64_t table_row_stride,
+                     void* q_out, int64_t q_out_stride_b, int64_t q_out_stride_s, int64_t q_out_stride_h,
+                     void* k_out, int64_t k_out_stride_b, int64_t k_out_stride_s, int64_t k_out_stride_h,
+                     int64_t batch, int64_t seq_len, int64_t q_heads, int64_t k_heads, int64_t head_dim,
+                     int style, int dtype, void* stream);
+
+/*
  * SwiGLU activation: y = silu(gate) * up = (gate / (1 + exp(-gate))) * up,
  * evaluated in fp32 and rounded once. gate, up and y are n_rows x hidden_dim
  * with independent row strides, so the packed layout (one [M, 2F] buffer whose

@@ -77,6 +77,11 @@ def test_residual_rope_swiglu_argument_errors(lib) -> None:
     assert rope(p, 0, 0, 0, p, p, 4, p, 0, 0, 0, 1, 1, 1, 8, 0, 3, None) == 2  # dtype
     assert rope(p, 0, 0, 0, p, p, 2, p, 0, 0, 0, 1, 2, 1, 8, 0, 2, None) == 1  # table stride < D/2
     assert rope(None, 0, 0, 0, None, None, 0, None, 0, 0, 0, 0, 4, 2, 8, 0, 2, None) == 0  # empty batch
+    qk = lib.ako_b200_rope_qk
+    assert qk(p, 0, 0, 0, p, 0, 0, 0, p, p, 4, p, 0, 0, 0, p, 0, 0, 0, 1, 1, 2, 1, 8, 7, 2, None) == 1  # style
+    assert qk(p, 0, 0, 0, p, 0, 0, 0, p, p, 4, p, 0, 0, 0, p, 0, 0, 0, 1, 1, -1, 1, 8, 0, 2, None) == 1  # heads
+    assert qk(p, 0, 0, 0, None, 0, 0, 0, p, p, 4, p, 0, 0, 0, None, 0, 0, 0, 1, 1, 2, 1, 8, 0, 2, None) == 1
+    assert qk(None, 0, 0, 0, None, 0, 0, 0, p, p, 4, None, 0, 0, 0, None, 0, 0, 0, 1, 1, 0, 0, 8, 0, 2, None) == 0
     assert lib.ako_b200_swiglu(p, 8, p, 8, p, 8, 2, 8, 5, None) == 2
     assert lib.ako_b200_swiglu(p, 4, p, 8, p, 8, 2, 8, 2, None) == 1
     assert lib.ako_b200_swiglu(None, 0, None, 0, None, 0, 0, 8, 2, None) == 0
@@ -98,8 +103,10 @@ def test_launch_override_validation(lib) -> None:
         lambda: kernels.rmsnorm_residual_cuda_sm100(torch.randn(2, 8), torch.randn(2, 8), torch.ones(8)),
         lambda: kernels.rope_cuda_sm100(torch.randn(1, 2, 1, 8), torch.ones(2, 4), torch.zeros(2, 4)),
         lambda: kernels.swiglu_cuda_sm100(torch.randn(2, 8), torch.randn(2, 8)),
+        lambda: kernels.rope_qk_cuda_sm100(torch.randn(1, 2, 4, 8), torch.randn(1, 2, 2, 8), torch.ones(2, 4),
+                                           torch.zeros(2, 4)),
     ],
-    ids=["rmsnorm", "rmsnorm_residual", "rope", "swiglu"],
+    ids=["rmsnorm", "rmsnorm_residual", "rope", "swiglu", "rope_qk"],
 )
 def test_wrappers_refuse_cpu_tensors(call) -> None:
     with pytest.raises(ValueError, match="requires a CUDA tensor"):

@@ -223,6 +223,43 @@ def test_rope_many_positions(cuda_device) -> None:
     np.testing.assert_array_equal(to_numpy(y), C.rope(x, cos, sin, "neox", O.BF16))
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("style", O.ROPE_STYLES)
+def test_rope_qk_fused_matches_two_ropes(cuda_device, dtype: str, style: str) -> None:
+    """One launch for q (32 heads) and k (8 heads) equals two rope calls and the
+    oracle, bit for bit; q passed as a (B, H, S, D) transposed view, k dense,
+    decode-style table slice."""
+    rng = np.random.default_rng(23)
+    cos_full, sin_full = O.build_rope_tables(8192, 128)
+    for b, s, off in ((4, 1, 2047), (2, 33, 0), (1, 5, 100)):
+        q_np = normal(rng, (b, 32, s, 128), 0, 1, dtype)  # (B, H, S, D) storage
+        k_np = normal(rng, (b, s, 8, 128), 0, 1, dtype)
+        q = to_torch(q_np, dtype, cuda_device).transpose(1, 2)
+        k = to_torch(k_np, dtype, cuda_device)
+        cos = to_torch(cos_full, O.F32, cuda_device)[off:off + s]
+        sin = to_torch(sin_full, O.F32, cuda_device)[off:off + s]
+        qo, ko = kernels.rope_qk_cuda_sm100(q, k, cos, sin, style)
+        assert qo.stride() == q.stride()
+        assert torch.equal(qo, kernels.rope_cuda_sm100(q, cos, sin, style))
+        assert torch.equal(ko, kernels.rope_cuda_sm100(k, cos, sin, style))
+        ref_q = O.rope(np.ascontiguousarray(q_np.transpose(0, 2, 1, 3)), cos_full[off:off + s],
+                       sin_full[off:off + s], style, dtype)
+        np.testing.assert_array_equal(to_numpy(qo), ref_q)
+        np.testing.assert_array_equal(to_numpy(ko), O.rope(k_np, cos_full[off:off + s], sin_full[off:off + s],
+                                                           style, dtype))
+
+
+def test_rope_qk_validation(cuda_device) -> None:
+    q = torch.randn(2, 4, 8, 64, device=cuda_device, dtype=torch.bfloat16)
+    cos = torch.ones(4, 32, device=cuda_device)
+    with pytest.raises(ValueError):
+        kernels.rope_qk_cuda_sm100(q, q[:, :3], cos, cos)
+    with pytest.raises(ValueError):
+        kernels.rope_qk_cuda_sm100(q, q.float(), cos, cos)
+    qo, ko = kernels.rope_qk_cuda_sm100(q, q[:, :, :0], cos, torch.zeros_like(cos))
+    assert torch.equal(qo, q) and ko.shape == (2, 4, 0, 64)
+
+
 def test_rope_position_zero_identity_and_empty(cuda_device) -> None:
     x = torch.randn(2, 3, 4, 64, device=cuda_device, dtype=torch.bfloat16)
     cos = torch.ones(3, 32, device=cuda_device)
