@@ -1,0 +1,249 @@
+"""LLaMA-style decoder with RMSNorm, RoPE and SwiGLU on the sm_100a kernels.
+
+The caller of the hot path that BASELINE config 5 measures (reference:
+``ako/models/decoder.py:37-335``): a stack of pre-norm blocks —
+``norm -> attention -> norm -> SwiGLU MLP`` with the residual carried through
+the fused residual-add RMSNorm — plus the token embedding and LM head the
+reference's stack leaves to its harness. Same configuration fields and
+norm/residual order as the reference; the layout is chosen for B200:
+
+* q, k and v come out of one packed GEMM and stay views of it; the fused
+  ``rope_qk`` kernel reads q and k in place and writes the rotated keys
+  straight into the KV cache (output strides are free in the C ABI);
+* gate and up come out of one packed GEMM; the SwiGLU kernel reads the two
+  halves in place;
+* the KV cache is preallocated ``(batch, kv_heads, max_len, head_dim)`` per
+  layer and written in place, where the reference concatenates the whole
+  cache every step (``ako/models/decoder.py:84-93``);
+* grouped-query attention goes through SDPA with ``enable_gqa`` instead of
+  materializing repeated heads (``ako/models/decoder.py:180-182``).
+
+GEMMs and attention are torch's (cuBLAS / SDPA), as config 5 specifies.
+``backend="torch"`` runs the same stack with the unfused reference math for
+RMSNorm, RoPE and SwiGLU (``ako_b200.dispatch.references``), for comparison.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Literal
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ako_b200 import _native, kernels
+from ako_b200.dispatch import references as refs
+
+Backend = Literal["b200", "torch"]
+
+
+@dataclass
+class ModelConfig:
+    """Shape of the stack (fields of the reference's ``ModelConfig``, plus vocab)."""
+
+    hidden_dim: int = 4096
+    n_layers: int = 4
+    n_heads: int = 32
+    n_kv_heads: int = 8
+    intermediate_dim: int = 11008
+    max_seq_len: int = 8192
+    rope_base: float = 10000.0
+    rope_style: str = "neox"
+    eps: float = 1e-5
+    vocab_size: int = 32000
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_dim // self.n_heads
+
+    def __post_init__(self) -> None:
+        if self.hidden_dim % self.n_heads:
+            raise ValueError(f"hidden_dim {self.hidden_dim} is not divisible by n_heads {self.n_heads}")
+        if self.n_heads % self.n_kv_heads:
+            raise ValueError(f"n_heads {self.n_heads} is not divisible by n_kv_heads {self.n_kv_heads}")
+        if self.head_dim % 2:
+            raise ValueError(f"head_dim {self.head_dim} must be even for RoPE")
+
+
+class KVCache:
+    """Preallocated per-layer keys and values, ``(batch, kv_heads, max_len, head_dim)``."""
+
+    def __init__(self, config: ModelConfig, batch: int, max_len: int, *, device, dtype) -> None:
+        shape = (batch, config.n_kv_heads, max_len, config.head_dim)
+        self.k = [torch.empty(shape, device=device, dtype=dtype) for _ in range(config.n_layers)]
+        self.v = [torch.empty(shape, device=device, dtype=dtype) for _ in range(config.n_layers)]
+        self.length = 0
+        self.max_len = max_len
+
+    def slot(self, layer: int, start: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Writable ``(batch, n, kv_heads, head_dim)`` views of positions ``[start, start + n)``."""
+        if start + n > self.max_len:
+            raise ValueError(f"KV cache holds {self.max_len} positions, asked for {start + n}")
+        return (self.k[layer][:, :, start:start + n].transpose(1, 2),
+                self.v[layer][:, :, start:start + n].transpose(1, 2))
+
+    def view(self, layer: int, end: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.k[layer][:, :, :end], self.v[layer][:, :, :end]
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, backend: Backend) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.backend = backend
+        d, hd = cfg.hidden_dim, cfg.head_dim
+        self.q_dim = cfg.n_heads * hd
+        self.kv_dim = cfg.n_kv_heads * hd
+        self.input_norm_weight = nn.Parameter(torch.ones(d))
+        self.post_attention_norm_weight = nn.Parameter(torch.ones(d))
+        self.qkv_proj = nn.Linear(d, self.q_dim + 2 * self.kv_dim, bias=False)
+        self.o_proj = nn.Linear(self.q_dim, d, bias=False)
+        self.gate_up_proj = nn.Linear(d, 2 * cfg.intermediate_dim, bias=False)
+        self.down_proj = nn.Linear(cfg.intermediate_dim, d, bias=False)
+
+    # -------------------------------------------------------- hot-path ops
+    def _norm(self, x, residual, weight):
+        eps = self.cfg.eps
+        if self.backend == "b200":
+            if residual is None:
+                return kernels.rmsnorm_cuda_sm100(x, weight, eps), x
+            return kernels.rmsnorm_residual_cuda_sm100(x, residual, weight, eps)
+        if residual is None:
+            return refs.rmsnorm_ref(x, weight, eps), x
+        return refs.rmsnorm_residual_ref(x, residual, weight, eps)
+
+    def _rope(self, q, k, cos, sin, k_dest):
+        style = self.cfg.rope_style
+        if self.backend == "b200":
+            if k_dest is None:
+                return kernels.rope_qk_cuda_sm100(q, k, cos, sin, style)
+            q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+            rope_qk_into(q, k, cos, sin, style, q_out, k_dest)
+            return q_out, k_dest
+        q_out, k_out = refs.rope_ref(q, cos, sin, style), refs.rope_ref(k, cos, sin, style)
+        if k_dest is not None:
+            k_dest.copy_(k_out)
+            k_out = k_dest
+        return q_out, k_out
+
+    def _swiglu(self, gu):
+        f = self.cfg.intermediate_dim
+        gate, up = gu[..., :f], gu[..., f:]
+        if self.backend == "b200":
+            return kernels.swiglu_cuda_sm100(gate, up)
+        return refs.swiglu_ref(gate, up)
+
+    # --------------------------------------------------------------- block
+    def forward(self, x, residual, cos, sin, cache: KVCache | None, layer: int):
+        cfg = self.cfg
+        b, s, _ = x.shape
+        h, residual = self._norm(x, residual, self.input_norm_weight)
+        qkv = self.qkv_proj(h)
+        q = qkv[..., : self.q_dim].view(b, s, cfg.n_heads, cfg.head_dim)
+        k = qkv[..., self.q_dim : self.q_dim + self.kv_dim].view(b, s, cfg.n_kv_heads, cfg.head_dim)
+        v = qkv[..., self.q_dim + self.kv_dim :].view(b, s, cfg.n_kv_heads, cfg.head_dim)
+        start = cache.length if cache is not None else 0
+        if s > 1 and start > 0:
+            raise NotImplementedError("chunked prefill onto a non-empty cache is not supported")
+        k_dest = v_dest = None
+        if cache is not None:
+            k_dest, v_dest = cache.slot(layer, start, s)
+        q, k = self._rope(q, k, cos, sin, k_dest)
+        if cache is not None:
+            v_dest.copy_(v)
+            keys, values = cache.view(layer, start + s)
+        else:
+            keys, values = k.transpose(1, 2), v.transpose(1, 2)
+        attn = F.scaled_dot_product_attention(
+            q.transpose(1, 2), keys, values, is_causal=s > 1 and start == 0, enable_gqa=True
+        )
+        out = self.o_proj(attn.transpose(1, 2).reshape(b, s, self.q_dim))
+        h, residual = self._norm(out, residual, self.post_attention_norm_weight)
+        return self.down_proj(self._swiglu(self.gate_up_proj(h))), residual
+
+
+class Decoder(nn.Module):
+    """Embedding -> decoder stack -> final RMSNorm -> LM head."""
+
+    def __init__(self, cfg: ModelConfig, backend: Backend = "b200") -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.backend = backend
+        self.embed = nn.Embedding(cfg.vocab_size, cfg.hidden_dim)
+        self.layers = nn.ModuleList(DecoderLayer(cfg, backend) for _ in range(cfg.n_layers))
+        self.final_norm_weight = nn.Parameter(torch.ones(cfg.hidden_dim))
+        self.lm_head = nn.Linear(cfg.hidden_dim, cfg.vocab_size, bias=False)
+        self._tables: tuple[torch.Tensor, torch.Tensor] | None = None
+
+    def rope_tables(self, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp32 tables for positions ``[0, max_seq_len)``, built once, sliced per call."""
+        if self._tables is None or self._tables[0].device != torch.device(device):
+            self._tables = refs.build_rope_tables(self.cfg.max_seq_len, self.cfg.head_dim,
+                                                  base=self.cfg.rope_base, device=device)
+        return self._tables
+
+    def new_cache(self, batch: int, max_len: int | None = None) -> KVCache:
+        p = self.embed.weight
+        return KVCache(self.cfg, batch, max_len or self.cfg.max_seq_len, device=p.device, dtype=p.dtype)
+
+    def hidden(self, ids: torch.Tensor, cache: KVCache | None = None) -> torch.Tensor:
+        """Final-normed hidden states ``(batch, seq, hidden)`` of token ids ``(batch, seq)``."""
+        s = ids.shape[1]
+        start = cache.length if cache is not None else 0
+        cos, sin = self.rope_tables(ids.device)
+        cos, sin = cos[start:start + s], sin[start:start + s]
+        x = self.embed(ids)
+        residual = None
+        for i, layer in enumerate(self.layers):
+            x, residual = layer(x, residual, cos, sin, cache, i)
+        if cache is not None:
+            cache.length = start + s
+        if self.backend == "b200":
+            out, _ = kernels.rmsnorm_residual_cuda_sm100(x, residual, self.final_norm_weight, self.cfg.eps)
+        else:
+            out, _ = refs.rmsnorm_residual_ref(x, residual, self.final_norm_weight, self.cfg.eps)
+        return out
+
+    def forward(self, ids: torch.Tensor, cache: KVCache | None = None) -> torch.Tensor:
+        """Logits of the last position of each sequence, ``(batch, vocab)``."""
+        return self.lm_head(self.hidden(ids, cache)[:, -1])
+
+
+def build_decoder(cfg: ModelConfig, *, backend: Backend = "b200", device="cuda", dtype=torch.bfloat16,
+                  seed: int = 0, std: float = 0.02) -> Decoder:
+    """Decoder with reproducible N(0, std) projection/embedding weights and unit norm weights."""
+    device = torch.device(device)
+    with torch.device("meta"):
+        model = Decoder(cfg, backend)
+    model = model.to_empty(device=device).to(dtype)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "norm_weight" in name:
+                p.fill_(1.0)
+            else:
+                p.copy_(torch.randn(p.shape, generator=gen, device=device, dtype=torch.float32) * std)
+    return model.eval()
+
+
+def rope_qk_into(q, k, cos, sin, style, q_out, k_out) -> None:
+    """``rope_qk`` writing into caller-provided views (e.g. a KV-cache slot)."""
+    fn = "rope_qk_into"
+    cos, sin = kernels._rope_tables(cos, sin)
+    code = kernels._dtype_code(q, "q", fn)
+    for t in (q, k, q_out, k_out):
+        if t.stride(-1) != 1 or not t.is_cuda:
+            raise ValueError(f"{fn}: CUDA tensors with a contiguous last axis required")
+    if q_out.shape != q.shape or k_out.shape != k.shape:
+        raise ValueError(f"{fn}: output shapes must match the inputs")
+    b, s, qh, d = q.shape
+    status = _native.lib().ako_b200_rope_qk(
+        q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+        k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+        cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+        q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_out.stride(2),
+        k_out.data_ptr(), k_out.stride(0), k_out.stride(1), k_out.stride(2),
+        b, s, qh, k.shape[2], d, kernels._STYLE_CODE[style], code, kernels._stream(q.device),
+    )
+    _native.raise_for_status(status, fn)

@@ -133,36 +133,25 @@ class Workload:
 
 
 # -------------------------------------------------------------- distributed
-def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import torch.distributed as dist
+def dist_setup() -> tuple[int, int, int]:
+    from ako_b200 import sharding
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
+    world, rank, local = sharding.env_world()
+    torch.cuda.set_device(local)
+    sharding.init("nccl", device=torch.device("cuda", local))
     return world, rank, local
 
 
 def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
+    from ako_b200 import sharding
 
-        dist.barrier()
+    sharding.barrier()
 
 
 def max_over_ranks(v: float, world: int, device: torch.device) -> float:
-    if world == 1:
-        return v
-    import torch.distributed as dist
+    from ako_b200 import sharding
 
-    t = torch.tensor([v], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return sharding.max_over_ranks(v, device)
 
 
 def timed_region(step, k: int, w: int, world: int) -> float:
@@ -373,10 +362,9 @@ def main() -> None:
     if world == 1 and not args.no_ops:
         ops = run_ops(device, peak)
 
-    if world > 1:
-        import torch.distributed as dist
+    from ako_b200 import sharding
 
-        dist.destroy_process_group()
+    sharding.finish()
     if rank != 0:
         return
 
