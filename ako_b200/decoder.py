@@ -163,6 +163,33 @@ class DecoderLayer(nn.Module):
         return self.down_proj(self._swiglu(self.gate_up_proj(h))), residual
 
 
+    def forward_static(self, x, residual, cos, sin, cache: "KVCache", layer: int, pos: torch.Tensor,
+                       mask: torch.Tensor):
+        """One decode step with shapes fixed for CUDA-graph capture.
+
+        ``pos`` is a one-element device tensor holding the write position; the
+        new key and value go into the cache with ``index_copy_`` at ``pos`` and
+        attention runs over the whole preallocated cache under ``mask``
+        (``(1, 1, 1, max_len)``, true up to ``pos``), so nothing depends on
+        host-side lengths.
+        """
+        cfg = self.cfg
+        b = x.shape[0]
+        h, residual = self._norm(x, residual, self.input_norm_weight)
+        qkv = self.qkv_proj(h)
+        q = qkv[..., : self.q_dim].view(b, 1, cfg.n_heads, cfg.head_dim)
+        k = qkv[..., self.q_dim : self.q_dim + self.kv_dim].view(b, 1, cfg.n_kv_heads, cfg.head_dim)
+        v = qkv[..., self.q_dim + self.kv_dim :].view(b, 1, cfg.n_kv_heads, cfg.head_dim)
+        q, k = self._rope(q, k, cos, sin, None)
+        cache.k[layer].index_copy_(2, pos, k.transpose(1, 2))
+        cache.v[layer].index_copy_(2, pos, v.transpose(1, 2))
+        attn = F.scaled_dot_product_attention(q.transpose(1, 2), cache.k[layer], cache.v[layer], attn_mask=mask,
+                                              enable_gqa=True)
+        out = self.o_proj(attn.transpose(1, 2).reshape(b, 1, self.q_dim))
+        h, residual = self._norm(out, residual, self.post_attention_norm_weight)
+        return self.down_proj(self._swiglu(self.gate_up_proj(h))), residual
+
+
 class Decoder(nn.Module):
     """Embedding -> decoder stack -> final RMSNorm -> LM head."""
 
@@ -208,6 +235,81 @@ class Decoder(nn.Module):
     def forward(self, ids: torch.Tensor, cache: KVCache | None = None) -> torch.Tensor:
         """Logits of the last position of each sequence, ``(batch, vocab)``."""
         return self.lm_head(self.hidden(ids, cache)[:, -1])
+
+
+class GraphDecoder:
+    """Greedy decoding with each whole step captured in one CUDA graph.
+
+    A step — embedding, every layer, final norm, LM head, argmax — is one graph
+    replay: one launch instead of ~55, so the step runs at device speed rather
+    than at the speed of Python issuing kernels. The position lives on the
+    device and advances inside the graph; attention covers the preallocated
+    cache under a position mask, so the graph is valid for every step. Tokens
+    are written to ``tokens[:, step]`` on the device.
+    """
+
+    def __init__(self, model: "Decoder", cache: KVCache, first_token: torch.Tensor, steps: int) -> None:
+        self.model = model
+        self.cache = cache
+        dev = first_token.device
+        self.start = cache.length
+        self.pos = torch.tensor([cache.length], dtype=torch.int64, device=dev)
+        self.step_idx = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.tok = first_token.clone()
+        self.tokens = torch.zeros(first_token.shape[0], steps, dtype=torch.int64, device=dev)
+        self.arange = torch.arange(cache.max_len, device=dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.steps = steps
+
+    def _step(self) -> None:
+        m = self.model
+        cos_full, sin_full = m.rope_tables(self.tok.device)
+        cos = cos_full.index_select(0, self.pos)
+        sin = sin_full.index_select(0, self.pos)
+        mask = (self.arange <= self.pos).view(1, 1, 1, -1)
+        x = m.embed(self.tok)
+        residual = None
+        for i, layer in enumerate(m.layers):
+            x, residual = layer.forward_static(x, residual, cos, sin, self.cache, i, self.pos, mask)
+        if m.backend == "b200":
+            h, _ = kernels.rmsnorm_residual_cuda_sm100(x, residual, m.final_norm_weight, m.cfg.eps)
+        else:
+            h, _ = refs.rmsnorm_residual_ref(x, residual, m.final_norm_weight, m.cfg.eps)
+        nxt = m.lm_head(h[:, -1]).argmax(-1, keepdim=True)
+        self.tok.copy_(nxt)
+        self.tokens.index_copy_(1, self.step_idx, nxt)
+        self.pos.add_(1)
+        self.step_idx.add_(1)
+
+    def capture(self) -> None:
+        """Warm up on a side stream, then capture one step (the state is reset after)."""
+        self.reset()
+        side = torch.cuda.Stream(self.tok.device)
+        side.wait_stream(torch.cuda.current_stream(self.tok.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream(self.tok.device).wait_stream(side)
+        self.reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        self.reset()
+
+    def reset(self, first_token: torch.Tensor | None = None) -> None:
+        self.pos.fill_(self.start)
+        self.step_idx.zero_()
+        if first_token is not None:
+            self.tok.copy_(first_token)
+
+    def run(self, first_token: torch.Tensor) -> torch.Tensor:
+        """Greedy-decode ``steps`` tokens from the cached context; returns ``(batch, steps)``."""
+        if self.graph is None:
+            self.capture()
+        self.reset(first_token)
+        for _ in range(self.steps):
+            self.graph.replay()
+        return self.tokens
 
 
 def build_decoder(cfg: ModelConfig, *, backend: Backend = "b200", device="cuda", dtype=torch.bfloat16,

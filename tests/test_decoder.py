@@ -57,3 +57,30 @@ def test_b200_backend_matches_reference_backend(cuda_device) -> None:
         assert torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item() > 0.9999
     # cached decode equals the full forward on the kernel backend too
     assert (outs["b200"][1][:, 0] - outs["b200"][2][:, 32]).abs().max().item() < 0.05
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("backend", ["b200", "torch"])
+def test_graph_decode_matches_eager_decode(cuda_device, backend: str) -> None:
+    """Whole-step CUDA-graph decoding (device position, masked attention over
+    the full cache) produces the eager path's greedy tokens."""
+    from ako_b200.decoder import GraphDecoder
+
+    cfg = ModelConfig(**SMALL)
+    m = build_decoder(cfg, backend=backend, device=cuda_device, dtype=torch.float32, seed=5)
+    ids = torch.randint(0, cfg.vocab_size, (3, 20), generator=torch.Generator().manual_seed(2)).to(cuda_device)
+    with torch.inference_mode():
+        cache = m.new_cache(3, 32)
+        m.hidden(ids, cache)
+        tok = ids[:, -1:].clone()
+        eager = []
+        for _ in range(6):
+            tok = m(tok, cache).argmax(-1, keepdim=True)
+            eager.append(tok)
+        eager = torch.cat(eager, 1)
+        cache.length = 20
+        gd = GraphDecoder(m, cache, ids[:, -1:], 6)
+        graph_tokens = gd.run(ids[:, -1:]).clone()
+        again = gd.run(ids[:, -1:]).clone()
+    assert torch.equal(graph_tokens, eager)
+    assert torch.equal(again, eager)
