@@ -137,6 +137,9 @@ def dist_setup() -> tuple[int, int, int]:
     from ako_b200 import sharding
 
     world, rank, local = sharding.env_world()
+    # NCCL's own log lines (its version banner included) go to stderr, so the
+    # only line rank 0 writes to stdout is the JSON result.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     torch.cuda.set_device(local)
     sharding.init("nccl", device=torch.device("cuda", local))
     return world, rank, local
