@@ -137,11 +137,21 @@ def dist_setup() -> tuple[int, int, int]:
     from ako_b200 import sharding
 
     world, rank, local = sharding.env_world()
-    # NCCL's own log lines (its version banner included) go to stderr, so the
-    # only line rank 0 writes to stdout is the JSON result.
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     torch.cuda.set_device(local)
-    sharding.init("nccl", device=torch.device("cuda", local))
+    if world > 1:
+        # NCCL prints its version banner on stdout (fd 1) when a communicator
+        # comes up; point fd 1 at stderr until then, so the only line rank 0
+        # writes to stdout is the JSON result.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            sharding.init("nccl", device=torch.device("cuda", local))
+            sharding.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local
 
 
