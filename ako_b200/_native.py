@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int, _c_int]),
     "ako_b200_rope_set_launch": (_c_int, [_c_int]),
+    "ako_b200_rmsnorm_set_staging": (_c_int, [_c_int, _c_int, _c_int]),
+    "ako_b200_take_device_status": (_c_int, [ctypes.POINTER(ctypes.c_int)]),
 }
 
 ABI_VERSION = 2
@@ -108,3 +110,10 @@ def raise_for_status(status: int, op: str) -> None:
     if status in (ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED_DTYPE):
         raise ValueError(f"{op}: {message}")
     raise RuntimeError(f"{op}: {message}")
+
+
+def take_device_status() -> int:
+    """Read and clear the kernels' device status word (0 = no bounded wait ran out)."""
+    value = ctypes.c_int(0)
+    raise_for_status(lib().ako_b200_take_device_status(ctypes.byref(value)), "take_device_status")
+    return value.value

@@ -13,6 +13,21 @@ struct Shape {
 
 Shape g_override = {0, 0, 0};
 
+// Staging mode: 0 = built-in choice, 1 = row-resident kernel only,
+// 2 = staged (bulk-copy ring) kernel where it applies.
+int g_mode = 0;
+int g_stages = 0;
+int g_ctas_per_sm = 0;
+
+// Built-in choice between the row-resident and the staged kernel.
+bool use_staged(const RmsArgs& a, int es) {
+    if (g_mode == 1) return false;
+    if (g_mode == 2) return true;
+    (void)a;
+    (void)es;
+    return false;
+}
+
 // Launch shape for a row of `nvec` 16-byte vectors, from a sweep of every
 // built shape on B200 (bf16, fp16, fp32; 2048..16384 wide; 1 to 32768 rows).
 // One CTA per row with two vectors per thread streams best up to 512
@@ -44,6 +59,13 @@ bool pick_shape(int64_t nvec, Shape* out) {
 
 template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
+    if (vector_ok && use_staged(a, sizeof(T))) {
+        const int dtype = sizeof(T) == 4 ? AKO_B200_F32 : (std::is_same_v<T, __half> ? AKO_B200_F16 : AKO_B200_BF16);
+        const int stages = g_stages > 0 ? g_stages : 4;
+        const int ctas = g_ctas_per_sm > 0 ? g_ctas_per_sm : 2;
+        const int rc = launch_rms_staged(a, dtype, RES, stages, ctas, st);
+        if (rc >= 0) return rc;
+    }
     if (vector_ok) {
         constexpr int VEC = 16 / sizeof(T);
         Shape s;
@@ -163,4 +185,22 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
                          cluster, threads_per_row, vectors_per_thread);
     g_override = {cluster, threads_per_row, vectors_per_thread};
     return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm) {
+    clear_error();
+    if (mode < 0 || mode > 2 || stages < 0 || stages > 8 || ctas_per_sm < 0 || ctas_per_sm > 8)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT,
+                         "rmsnorm staging (mode %d, %d stages, %d CTAs per SM) is out of range", mode, stages,
+                         ctas_per_sm);
+    g_mode = mode;
+    g_stages = stages;
+    g_ctas_per_sm = ctas_per_sm;
+    return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_take_device_status(int* status) {
+    clear_error();
+    if (status == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "status is a null pointer");
+    return take_staged_status(status);
 }

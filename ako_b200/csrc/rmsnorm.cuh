@@ -297,6 +297,13 @@ int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
     return check_launch(RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)");
 }
 
+// Persistent variant with rows staged in shared memory by bulk copies
+// (rmsnorm_tma.cu); -1 when the row is too wide for it.
+int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st);
+
+// Reads and clears the staged kernels' device status word (synchronizing).
+int take_staged_status(int* status);
+
 // Instantiated once per dtype in rmsnorm_{f32,f16,bf16}.cu (compiled in parallel).
 #define AKO_RMS_DECLARE(T, KW)                                                        \
     KW template int launch_rms_rows<T, false>(const RmsArgs&, int, int, int, cudaStream_t); \

@@ -1,0 +1,234 @@
+// RMSNorm / fused residual RMSNorm with rows staged in shared memory by 1-D
+// bulk copies (cp.async.bulk, mbarrier completion): a persistent kernel for
+// row counts too small to keep HBM busy with one short-lived CTA per row.
+//
+// Each CTA owns rows blockIdx.x, blockIdx.x + gridDim.x, ... and a ring of
+// `stages` shared-memory slots. Thread 0 keeps up to `stages` rows in flight
+// (x, and the residual when fused); all threads wait on the slot's mbarrier,
+// read their 16-byte vectors into registers, and the slot is refilled with
+// the row `stages` ahead as soon as the reduction's barrier shows every
+// thread has read it. Arithmetic, summation order and rounding are those of
+// rms_rows_kernel (same results bit for bit).
+//
+// Every wait is bounded: if a copy never completes, the CTA records
+// kStatusWaitTimeout in g_tma_status, waits (bounded) for its other copies,
+// and leaves without writing the row.
+#include <climits>
+
+#include "rmsnorm.cuh"
+
+namespace ako_b200 {
+
+__device__ int g_tma_status = 0;
+
+namespace {
+
+constexpr int kTmaThreads = 256;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kWaitPolls = 1u << 24;   // ~a second of polling
+constexpr uint32_t kDrainPolls = 1u << 20;
+
+struct TmaArgs {
+    RmsArgs a;
+    int stages;
+    int stage_bytes;  // x row (+ residual row), multiple of 16
+};
+
+template <typename T, int NV, bool RES>
+__global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
+    constexpr int VEC = 16 / sizeof(T);
+    constexpr int WARPS = kTmaThreads / 32;
+    using P = Packed<T, VEC>;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ uint64_t full[kMaxStages];
+    __shared__ float scratch[2][WARPS];
+    const RmsArgs& a = t.a;
+    const int h = a.h;
+    const uint32_t row_bytes = static_cast<uint32_t>(h) * sizeof(T);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < t.stages; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int slot, int64_t row) {
+        unsigned char* dst = ring + static_cast<size_t>(slot) * t.stage_bytes;
+        mbar_expect_tx(&full[slot], RES ? 2 * row_bytes : row_bytes);
+        bulk_load(dst, static_cast<const T*>(a.x) + row * a.sx, row_bytes, &full[slot]);
+        if constexpr (RES) bulk_load(dst + row_bytes, static_cast<const T*>(a.r) + row * a.sr, row_bytes, &full[slot]);
+    };
+
+    const int64_t first = blockIdx.x;
+    const int64_t step = gridDim.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < t.stages; ++s) {
+            const int64_t row = first + s * step;
+            if (row < a.rows) issue(s, row);
+        }
+    }
+
+    int k = 0;
+    for (int64_t row = first; row < a.rows; row += step, ++k) {
+        const int slot = k % t.stages;
+        const uint32_t phase = static_cast<uint32_t>(k / t.stages) & 1u;
+        const bool ok = mbar_wait_bounded(&full[slot], phase, kWaitPolls);
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0) {
+                atomicExch(&g_tma_status, kStatusWaitTimeout);
+                // Let the copies this CTA started land before it exits.
+                for (int j = 0; j < t.stages; ++j) {
+                    const int64_t r2 = row + j * step;
+                    if (r2 < a.rows)
+                        mbar_wait_bounded(&full[(k + j) % t.stages],
+                                          static_cast<uint32_t>((k + j) / t.stages) & 1u, kDrainPolls);
+                }
+            }
+            return;
+        }
+
+        const unsigned char* base = ring + static_cast<size_t>(slot) * t.stage_bytes;
+        const T* xs = reinterpret_cast<const T*>(base);
+        P v[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            if (col < h) v[j] = *reinterpret_cast<const P*>(xs + col);
+        }
+        if constexpr (RES) {
+            const T* rs = reinterpret_cast<const T*>(base + row_bytes);
+            T* ro = static_cast<T*>(a.ro) + row * a.sro;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+                if (col < h) {
+                    const P rv = *reinterpret_cast<const P*>(rs + col);
+#pragma unroll
+                    for (int e = 0; e < VEC; e += 2) {
+                        const float2 xa = get2<T, VEC>(v[j], e);
+                        const float2 ra = get2<T, VEC>(rv, e);
+                        put2<T, VEC>(v[j], e, __fadd_rn(xa.x, ra.x), __fadd_rn(xa.y, ra.y));
+                    }
+                    st_global<T, VEC>(ro + col, v[j]);
+                }
+            }
+        }
+        float part[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            float sq[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 f = get2<T, VEC>(v[j], e);
+                sq[e] = __fmul_rn(f.x, f.x);
+                sq[e + 1] = __fmul_rn(f.y, f.y);
+            }
+            part[j] = col < h ? tree_sum<VEC>(sq) : 0.0f;
+        }
+        float w_sum = warp_sum(tree_sum<NV>(part));
+        float* sc = scratch[k & 1];
+        if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
+        __syncthreads();  // every thread has read the slot and published its warp's sum
+        if (threadIdx.x == 0) {
+            const int64_t next = row + static_cast<int64_t>(t.stages) * step;
+            if (next < a.rows) {
+                fence_proxy_async_smem();
+                issue(slot, next);
+            }
+        }
+        float parts[WARPS];
+#pragma unroll
+        for (int i = 0; i < WARPS; ++i) parts[i] = sc[i];
+        const float total = tree_sum<WARPS>(parts);
+        const float mean = __fdiv_rn(total, static_cast<float>(h));
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        T* yr = static_cast<T*>(a.y) + row * a.sy;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            if (col < h) {
+                float w[VEC];
+                load_weight_vec<VEC>(a.w, a.wdtype, col, w);
+                P o;
+#pragma unroll
+                for (int e = 0; e < VEC; e += 2) {
+                    const float2 f = get2<T, VEC>(v[j], e);
+                    put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w[e]), __fmul_rn(__fmul_rn(f.y, inv), w[e + 1]));
+                }
+                st_global<T, VEC>(yr + col, o);
+            }
+        }
+    }
+}
+
+template <typename T, int NV, bool RES>
+int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
+    const int row_bytes = a.h * static_cast<int>(sizeof(T));
+    TmaArgs t{a, stages, RES ? 2 * row_bytes : row_bytes};
+    const size_t smem = static_cast<size_t>(stages) * t.stage_bytes;
+    auto kernel = rms_tma_kernel<T, NV, RES>;
+    // Largest ring already allowed for this instantiation, per device.
+    static int configured_bytes[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    if (static_cast<int>(smem) > configured_bytes[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm(staged): %zu bytes of shared memory: %s", smem,
+                             cudaGetErrorString(e));
+        }
+        configured_bytes[dev] = static_cast<int>(smem);
+    }
+    int64_t grid = static_cast<int64_t>(sm_count()) * ctas_per_sm;
+    if (grid > a.rows) grid = a.rows;
+    kernel<<<static_cast<unsigned>(grid), kTmaThreads, smem, st>>>(t);
+    return check_launch(RES ? "rmsnorm_residual(staged)" : "rmsnorm(staged)");
+}
+
+template <typename T, bool RES>
+int launch_dtype(const RmsArgs& a, int nv, int stages, int ctas_per_sm, cudaStream_t st) {
+    switch (nv) {
+        case 1: return launch_one<T, 1, RES>(a, stages, ctas_per_sm, st);
+        case 2: return launch_one<T, 2, RES>(a, stages, ctas_per_sm, st);
+        case 4: return launch_one<T, 4, RES>(a, stages, ctas_per_sm, st);
+        case 8: return launch_one<T, 8, RES>(a, stages, ctas_per_sm, st);
+        default: return -1;
+    }
+}
+
+}  // namespace
+
+// Staged launch for rows of `h` 16-bit or fp32 elements (16-byte aligned rows,
+// h * sizeof(T) a multiple of 16); -1 when the row is too wide for it.
+int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st) {
+    const int es = dtype_size(dtype);
+    const int nvec = a.h * es / 16;
+    int nv = 1;
+    while (nv * kTmaThreads < nvec) nv *= 2;
+    if (nv > 8 || stages < 1 || stages > kMaxStages || ctas_per_sm < 1) return -1;
+    const int row_bytes = a.h * es;
+    if (static_cast<int64_t>(stages) * (res ? 2 : 1) * row_bytes > 200 * 1024) return -1;
+    switch (dtype) {
+        case AKO_B200_F32: return res ? launch_dtype<float, true>(a, nv, stages, ctas_per_sm, st)
+                                      : launch_dtype<float, false>(a, nv, stages, ctas_per_sm, st);
+        case AKO_B200_F16: return res ? launch_dtype<__half, true>(a, nv, stages, ctas_per_sm, st)
+                                      : launch_dtype<__half, false>(a, nv, stages, ctas_per_sm, st);
+        default: return res ? launch_dtype<__nv_bfloat16, true>(a, nv, stages, ctas_per_sm, st)
+                            : launch_dtype<__nv_bfloat16, false>(a, nv, stages, ctas_per_sm, st);
+    }
+}
+
+int take_staged_status(int* status) {
+    int value = 0;
+    const int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&value, g_tma_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_tma_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(AKO_B200_ERR_CUDA, "device status: %s", cudaGetErrorString(e));
+    *status = value;
+    return AKO_B200_OK;
+}
+
+}  // namespace ako_b200

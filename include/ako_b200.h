@@ -174,6 +174,25 @@ int ako_b200_swiglu(const void* gate, int64_t gate_row_stride,
 int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_per_thread);
 
 /*
+ * RMSNorm kernel choice for measurement sweeps: mode 1 uses the
+ * row-resident kernel only; mode 2 uses, where the row fits, the persistent
+ * kernel that stages rows in shared memory with 1-D bulk copies (`stages`
+ * rows in flight per CTA, `ctas_per_sm` CTAs per SM; 0 = defaults); mode 0
+ * restores the built-in choice. Not part of the reference's interface; it
+ * has no counterpart there. Process-wide, not thread-safe.
+ */
+int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm);
+
+/*
+ * Reads and clears the device status word of this library's kernels on the
+ * current device: 0, or 1 when a kernel's bounded wait for an asynchronous
+ * copy ran out (the kernel then left its rows unwritten). Synchronizes the
+ * device; meant for diagnostics and tests. Not part of the reference's
+ * interface; it has no counterpart there.
+ */
+int ako_b200_take_device_status(int* status);
+
+/*
  * Launch-shape override for measurement sweeps: each RoPE thread rotates
  * `heads_per_thread` heads (1, 2 or 4); 0 restores the built-in choice. Not
  * part of the reference's interface; it has no counterpart there.

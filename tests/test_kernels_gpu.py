@@ -141,6 +141,49 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
         lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_staged_rmsnorm_matches_oracle(cuda_device, dtype: str) -> None:
+    """The persistent bulk-copy kernel: every stage count and CTA density,
+    rows fewer than CTAs, many rows per CTA, strided rows, fp32 weights;
+    identical to the row-resident kernel, and no bounded wait ran out."""
+    lib = _native.lib()
+    rng = np.random.default_rng(31)
+    vec = 8 if dtype != O.F32 else 4
+    try:
+        for h in (vec, 256, 1000 if dtype == O.F32 else 1000 - 1000 % vec, 2048, 4096, 8192, 16384):
+            if h % vec or h * (4 if dtype == O.F32 else 2) > 32768:
+                continue
+            for rows, stages, ctas in ((1, 4, 2), (3, 1, 1), (300, 2, 1), (700, 8, 4), (1500, 3, 2)):
+                if rows * h > 4_000_000:
+                    rows = max(1, 4_000_000 // h)
+                x = normal(rng, (rows, h), 0, 1, dtype)
+                r = normal(rng, (rows, h), 0, 1, dtype)
+                w = normal(rng, (h,), 1, 0.1, dtype)
+                xt, rt, wt = (to_torch(a, dtype, cuda_device) for a in (x, r, w))
+                assert lib.ako_b200_rmsnorm_set_staging(2, stages, ctas) == 0
+                y_s, ro_s = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
+                y1_s = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
+                assert lib.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
+                y_r, ro_r = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
+                y1_r = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
+                assert torch.equal(y_s, y_r) and torch.equal(ro_s, ro_r) and torch.equal(y1_s, y1_r), (h, rows)
+                y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+                np.testing.assert_array_equal(to_numpy(ro_s), ro_ref)
+                assert_parity(y_ref, to_numpy(y_s), dtype, "rmsnorm_residual", f"staged h={h} rows={rows}")
+        # strided rows and an fp32 weight through the staged path
+        base = to_torch(normal(rng, (64, 4096 + 64), 0, 1, dtype), dtype, cuda_device)
+        xs = base[:, 64:]
+        wf = to_torch(normal(rng, (4096,), 1, 0.1, O.F32), O.F32, cuda_device)
+        assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
+        y = kernels.rmsnorm_cuda_sm100(xs, wf, 1e-6)
+        assert_parity(C.rmsnorm(to_numpy(xs), to_numpy(wf), 1e-6, dtype, O.F32), to_numpy(y), dtype, "rmsnorm",
+                      "staged strided")
+        torch.cuda.synchronize()
+        assert _native.take_device_status() == 0
+    finally:
+        lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+
+
 def test_rmsnorm_leading_dims_and_empty(cuda_device) -> None:
     rng = np.random.default_rng(9)
     x = normal(rng, (2, 3, 5, 512), 0, 1, O.BF16)
