@@ -7,8 +7,10 @@
 // (x, and the residual when fused); all threads wait on the slot's mbarrier,
 // read their 16-byte vectors into registers, and the slot is refilled with
 // the row `stages` ahead as soon as the reduction's barrier shows every
-// thread has read it. Arithmetic, summation order and rounding are those of
-// rms_rows_kernel (same results bit for bit).
+// thread has read it. Arithmetic and rounding are those of rms_rows_kernel;
+// the pairwise sum of squares is partitioned over 256 threads, so fp32
+// results can differ from a row-resident launch of another thread count in
+// the last bits (the rounded residual is identical).
 //
 // Every wait is bounded: if a copy never completes, the CTA records
 // kStatusWaitTimeout in g_tma_status, waits (bounded) for its other copies,
