@@ -144,6 +144,13 @@ struct FastDiv {
     }
 };
 
+// Starts fetching the L1 line holding element `i` of a runtime-typed weight
+// vector, so a later load_weight_vec of it hits L1.
+__device__ __forceinline__ void prefetch_weight(const void* w, int wdtype, int64_t i) {
+    const char* p = static_cast<const char*>(w) + i * (wdtype == AKO_B200_F32 ? 4 : 2);
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // ----------------------------------------------------------------- reductions
 // Butterfly over `WIDTH` lanes: every lane ends with the bitwise-identical sum
 // (fp32 addition is commutative, so partner pairs add the same two values).

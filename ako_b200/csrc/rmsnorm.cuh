@@ -77,6 +77,13 @@ rms_rows_kernel(const RmsArgs a) {
         const int col = (j * TPR + lane) * VEC;
         if (col < width) v[j] = ld_stream<T, VEC>(xr + col);
     }
+    // The weight is needed only after the reduction; start its fetch now so
+    // it is not a second memory round trip on the row's critical path.
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int col = (j * TPR + lane) * VEC;
+        if (col < width) prefetch_weight(a.w, a.wdtype, c0 + col);
+    }
 
     if constexpr (RES) {
         const T* rr = static_cast<const T*>(a.r) + row * a.sr + c0;
@@ -234,6 +241,7 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 32, 2) \
     AKO_RMS_CASE(T, RES, 1, 32, 4) \
     AKO_RMS_CASE(T, RES, 1, 32, 8) \
+    AKO_RMS_CASE(T, RES, 1, 64, 1) \
     AKO_RMS_CASE(T, RES, 1, 64, 2) \
     AKO_RMS_CASE(T, RES, 1, 64, 4) \
     AKO_RMS_CASE(T, RES, 1, 64, 8) \
@@ -254,28 +262,37 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 1024, 4) \
     AKO_RMS_CASE(T, RES, 1, 1024, 8) \
     AKO_RMS_CASE(T, RES, 2, 64, 4) \
+    AKO_RMS_CASE(T, RES, 2, 128, 1) \
     AKO_RMS_CASE(T, RES, 2, 128, 2) \
     AKO_RMS_CASE(T, RES, 2, 128, 4) \
+    AKO_RMS_CASE(T, RES, 2, 256, 1) \
     AKO_RMS_CASE(T, RES, 2, 256, 2) \
     AKO_RMS_CASE(T, RES, 2, 256, 4) \
+    AKO_RMS_CASE(T, RES, 2, 512, 1) \
     AKO_RMS_CASE(T, RES, 2, 512, 2) \
     AKO_RMS_CASE(T, RES, 2, 512, 4) \
     AKO_RMS_CASE(T, RES, 2, 1024, 1) \
     AKO_RMS_CASE(T, RES, 2, 1024, 2) \
     AKO_RMS_CASE(T, RES, 4, 64, 4) \
+    AKO_RMS_CASE(T, RES, 4, 128, 1) \
     AKO_RMS_CASE(T, RES, 4, 128, 2) \
     AKO_RMS_CASE(T, RES, 4, 128, 4) \
+    AKO_RMS_CASE(T, RES, 4, 256, 1) \
     AKO_RMS_CASE(T, RES, 4, 256, 2) \
     AKO_RMS_CASE(T, RES, 4, 256, 4) \
+    AKO_RMS_CASE(T, RES, 4, 512, 1) \
     AKO_RMS_CASE(T, RES, 4, 512, 2) \
     AKO_RMS_CASE(T, RES, 4, 512, 4) \
     AKO_RMS_CASE(T, RES, 4, 1024, 1) \
     AKO_RMS_CASE(T, RES, 4, 1024, 2) \
     AKO_RMS_CASE(T, RES, 8, 64, 4) \
+    AKO_RMS_CASE(T, RES, 8, 128, 1) \
     AKO_RMS_CASE(T, RES, 8, 128, 2) \
     AKO_RMS_CASE(T, RES, 8, 128, 4) \
+    AKO_RMS_CASE(T, RES, 8, 256, 1) \
     AKO_RMS_CASE(T, RES, 8, 256, 2) \
     AKO_RMS_CASE(T, RES, 8, 256, 4) \
+    AKO_RMS_CASE(T, RES, 8, 512, 1) \
     AKO_RMS_CASE(T, RES, 8, 512, 2) \
     AKO_RMS_CASE(T, RES, 8, 512, 4) \
     AKO_RMS_CASE(T, RES, 8, 1024, 1) \

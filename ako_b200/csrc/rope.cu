@@ -205,9 +205,13 @@ template <typename T>
 int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st, const char* name) {
     constexpr int VEC = 16 / sizeof(T);
     const int heads = a.t0.heads + a.t1.heads;
-    // Heads per thread: two heads share a thread's table values and keep
-    // more loads in flight (measured fastest for 8..40 heads at D = 128).
-    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (heads >= 8 ? 2 : 1);
+    // Heads per thread: two heads share a thread's table values and keep more
+    // loads in flight, which is fastest once the grid fills the GPU (8..40
+    // heads at D = 128); a grid smaller than one wave of threads (decode:
+    // a few positions) finishes sooner with one head per thread.
+    const int64_t threads_one_head = a.n_pos * heads * (a.half / (interleaved ? VEC / 2 : VEC));
+    const bool small = threads_one_head < static_cast<int64_t>(sm_count()) * 2048;
+    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : ((heads >= 8 && !small) ? 2 : 1);
     const int chunk_pairs = interleaved ? VEC / 2 : VEC;
     if (vector_ok && a.half % chunk_pairs == 0 && a.half / chunk_pairs <= 256) {
         if (interleaved) return launch_vec<T, VEC / 2, true>(a, hpt, st, name);

@@ -39,7 +39,10 @@ struct SwigluArgs {
     FastDiv row_div;  // divides by per_row (valid when total < 2^32)
 };
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;  // default CTA size
+
+int g_threads = 0;  // tuning override of the CTA size (0: built-in)
+int g_unroll = 0;   // tuning override of vectors in flight per thread (0: built-in)
 
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
@@ -60,20 +63,20 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // FLAT: all three operands are dense (row stride == hidden_dim), so vector
 // i sits at element i * VEC of each. Otherwise rows come from FastDiv
 // (NARROW, total < 2^32) or a 64-bit division.
-template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW>
-__global__ void __launch_bounds__(kThreads, 4) swiglu_kernel(const SwigluArgs a) {
+template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW, int THREADS>
+__global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
     using P = Packed<T, VEC>;
     const T* gp = static_cast<const T*>(a.g);
     const T* up = static_cast<const T*>(a.u);
     T* yp = static_cast<T*>(a.y);
-    const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads * UNROLL;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads * UNROLL + threadIdx.x; base < a.total;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * THREADS * UNROLL;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * THREADS * UNROLL + threadIdx.x; base < a.total;
          base += step) {
         P g[UNROLL], u[UNROLL];
         int64_t yo[UNROLL];
 #pragma unroll
         for (int k = 0; k < UNROLL; ++k) {
-            const int64_t i = base + static_cast<int64_t>(k) * kThreads;
+            const int64_t i = base + static_cast<int64_t>(k) * THREADS;
             if (i < a.total) {
                 int64_t go, uo;
                 if constexpr (FLAT) {
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 4) swiglu_kernel(const SwigluArgs a)
         }
 #pragma unroll
         for (int k = 0; k < UNROLL; ++k) {
-            const int64_t i = base + static_cast<int64_t>(k) * kThreads;
+            const int64_t i = base + static_cast<int64_t>(k) * THREADS;
             if (i < a.total) {
                 P o;
                 if constexpr (VEC % 2 == 0) {
@@ -123,22 +126,41 @@ __global__ void __launch_bounds__(kThreads, 4) swiglu_kernel(const SwigluArgs a)
     }
 }
 
-template <typename T, int VEC, int UNROLL>
+template <typename T, int VEC, int UNROLL, int THREADS>
 int launch(SwigluArgs a, bool flat, cudaStream_t st) {
-    const int64_t per_cta = static_cast<int64_t>(kThreads) * UNROLL;
+    const int64_t per_cta = static_cast<int64_t>(THREADS) * UNROLL;
     int64_t grid = (a.total + per_cta - 1) / per_cta;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 CTAs of 256 threads fill an SM
+    const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / THREADS);  // a full SM's worth of threads each
     if (grid > cap) grid = cap;
     const unsigned g = static_cast<unsigned>(grid);
     if (flat) {
-        swiglu_kernel<T, VEC, UNROLL, true, true><<<g, kThreads, 0, st>>>(a);
+        swiglu_kernel<T, VEC, UNROLL, true, true, THREADS><<<g, THREADS, 0, st>>>(a);
     } else if (a.total <= static_cast<int64_t>(UINT_MAX)) {
         a.row_div = FastDiv::make(static_cast<uint32_t>(a.per_row));
-        swiglu_kernel<T, VEC, UNROLL, false, true><<<g, kThreads, 0, st>>>(a);
+        swiglu_kernel<T, VEC, UNROLL, false, true, THREADS><<<g, THREADS, 0, st>>>(a);
     } else {
-        swiglu_kernel<T, VEC, UNROLL, false, false><<<g, kThreads, 0, st>>>(a);
+        swiglu_kernel<T, VEC, UNROLL, false, false, THREADS><<<g, THREADS, 0, st>>>(a);
     }
     return check_launch("swiglu");
+}
+
+template <typename T, int VEC>
+int launch_vec(const SwigluArgs& a, bool flat, cudaStream_t st) {
+    // Large problems keep two vectors per thread in flight in 256-thread CTAs;
+    // small ones (decode rows) use one vector per thread in 64-thread CTAs, so
+    // the few vectors spread over as many SMs as possible.
+    const bool small = a.total < static_cast<int64_t>(sm_count()) * kThreads * 4;
+    const int threads = g_threads > 0 ? g_threads : (small ? 64 : kThreads);
+    const int unroll = g_unroll > 0 ? g_unroll : (small ? 1 : 2);
+    switch (threads * 16 + unroll) {
+        case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, st);
+        case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, st);
+        case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, st);
+        case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, st);
+        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, st);
+        case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, st);
+        default: return launch<T, VEC, 2, 256>(a, flat, st);
+    }
 }
 
 template <typename T>
@@ -147,14 +169,11 @@ int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaSt
     if (vector_ok) {
         a.per_row = h / VEC;
         a.total = rows * a.per_row;
-        // Small problems (decode rows) spread over more CTAs; large ones keep
-        // four vectors per thread in flight.
-        if (a.total < static_cast<int64_t>(sm_count()) * kThreads * 4) return launch<T, VEC, 1>(a, flat, st);
-        return launch<T, VEC, 2>(a, flat, st);
+        return launch_vec<T, VEC>(a, flat, st);
     }
     a.per_row = h;
     a.total = rows * h;
-    return launch<T, 1, 4>(a, flat, st);
+    return launch<T, 1, 4, 256>(a, flat, st);
 }
 
 }  // namespace
@@ -190,4 +209,17 @@ extern "C" int ako_b200_swiglu(const void* gate, int64_t gate_row_stride, const 
         case AKO_B200_F16: return run<__half>(a, n_rows, hidden_dim, vector_ok, flat, st);
         default: return run<__nv_bfloat16>(a, n_rows, hidden_dim, vector_ok, flat, st);
     }
+}
+
+extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {
+    clear_error();
+    const int key = threads * 16 + vectors_per_thread;
+    if (!(threads == 0 && vectors_per_thread == 0) && key != 64 * 16 + 1 && key != 64 * 16 + 2 &&
+        key != 128 * 16 + 1 && key != 128 * 16 + 2 && key != 256 * 16 + 1 && key != 256 * 16 + 2 &&
+        key != 256 * 16 + 4)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "swiglu launch (%d threads, %d vectors) is not built",
+                         threads, vectors_per_thread);
+    g_threads = threads;
+    g_unroll = vectors_per_thread;
+    return AKO_B200_OK;
 }

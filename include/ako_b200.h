@@ -200,6 +200,15 @@ int ako_b200_take_device_status(int* status);
  */
 int ako_b200_rope_set_launch(int heads_per_thread);
 
+/*
+ * Launch-shape override for measurement sweeps: SwiGLU CTAs of `threads`
+ * threads (64, 128 or 256), each keeping `vectors_per_thread` 16-byte vectors
+ * in flight (1, 2; 4 with 256 threads); (0, 0) restores the built-in choice.
+ * Not part of the reference's interface; it has no counterpart there.
+ * Process-wide, not thread-safe.
+ */
+int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
+
 #ifdef __cplusplus
 }
 #endif
