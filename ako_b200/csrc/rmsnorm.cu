@@ -28,18 +28,31 @@ bool use_staged(const RmsArgs& a, int es) {
     return false;
 }
 
-// Launch shape for a row of `nvec` 16-byte vectors, from a sweep of every
-// built shape on B200 (bf16, fp16, fp32; 2048..16384 wide; 1 to 32768 rows).
-// One CTA per row with two vectors per thread streams best up to 512
-// threads (1024-vector rows): its registers stay low enough for several
-// CTAs per SM, so loads of the next rows are in flight while a row reduces.
-// Wider rows keep 512-1024 threads with 4 vectors each. Rows wider than one
-// CTA's registers hold (8192 vectors) are split over a cluster of 8 CTAs;
-// splitting narrower rows measured slower at every row count.
-bool pick_shape(int64_t nvec, Shape* out) {
+// Launch shape for `rows` rows of `nvec` 16-byte vectors, from sweeps of
+// every built shape on B200 (bf16, fp16, fp32; 2048..16384 wide; 1 to 32768
+// rows; device time per call with the L2 cold, and inside CUDA graphs).
+//  * Many rows: one CTA per row with two vectors per thread up to 512
+//    threads (1024-vector rows): registers stay low enough for several CTAs
+//    per SM, so loads of the next rows are in flight while a row reduces.
+//    Wider rows keep 512-1024 threads with 4 vectors each; rows wider than
+//    one CTA's registers hold (8192 vectors) are split over a cluster of 8.
+//  * Few rows (decode): latency, not bandwidth, decides. One vector per
+//    thread (twice the threads) up to 512-vector rows; 2048-vector rows split
+//    over a cluster of 4 CTAs so a row's loads come from 4 SMs at once.
+bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
     const Shape& o = g_override;
     if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
         *out = o;
+        return true;
+    }
+    if (rows <= 512 && nvec > 32 && nvec <= 512) {
+        int tpr = 64;
+        while (tpr < nvec) tpr *= 2;
+        *out = Shape{1, tpr, 1};
+        return true;
+    }
+    if (nvec > 1024 && nvec <= 2048 && nvec % 4 == 0 && rows <= 64) {
+        *out = rows <= 32 ? Shape{4, 512, 1} : Shape{4, 256, 2};
         return true;
     }
     static const Shape table[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
@@ -69,7 +82,7 @@ int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok) {
         constexpr int VEC = 16 / sizeof(T);
         Shape s;
-        if (pick_shape(a.h / VEC, &s)) {
+        if (pick_shape(a.h / VEC, a.rows, &s)) {
             const int rc = launch_rms_rows<T, RES>(a, s.cluster, s.tpr, s.nv, st);
             if (rc >= 0) return rc;
         }
