@@ -182,10 +182,10 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
         g_override = {0, 0, 0};
         return AKO_B200_OK;
     }
-    static const int single[][2] = {{32, 1},  {32, 2},   {32, 4},   {32, 8},   {64, 1},  {64, 2},  {64, 4},  {64, 8},
-                                    {128, 1}, {128, 2},  {128, 4},  {128, 8},  {256, 1}, {256, 2}, {256, 4}, {256, 8},
-                                    {512, 1}, {512, 2},  {512, 4},  {512, 8},  {1024, 1}, {1024, 2}, {1024, 4},
-                                    {1024, 8}};
+    static const int single[][2] = {{32, 1},   {32, 2},   {32, 4},   {32, 8},   {32, 16},  {64, 1},  {64, 2},
+                                    {64, 4},   {64, 8},   {64, 16},  {128, 1},  {128, 2},  {128, 4}, {128, 8},
+                                    {128, 16}, {256, 1},  {256, 2},  {256, 4},  {256, 8},  {512, 1}, {512, 2},
+                                    {512, 4},  {512, 8},  {1024, 1}, {1024, 2}, {1024, 4}, {1024, 8}};
     static const int split[][2] = {{64, 4},  {128, 1}, {128, 2}, {128, 4}, {256, 1}, {256, 2},
                                    {256, 4}, {512, 1}, {512, 2}, {512, 4}, {1024, 1}, {1024, 2}};
     bool ok = false;

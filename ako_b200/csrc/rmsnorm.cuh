@@ -241,14 +241,17 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 32, 2) \
     AKO_RMS_CASE(T, RES, 1, 32, 4) \
     AKO_RMS_CASE(T, RES, 1, 32, 8) \
+    AKO_RMS_CASE(T, RES, 1, 32, 16) \
     AKO_RMS_CASE(T, RES, 1, 64, 1) \
     AKO_RMS_CASE(T, RES, 1, 64, 2) \
     AKO_RMS_CASE(T, RES, 1, 64, 4) \
     AKO_RMS_CASE(T, RES, 1, 64, 8) \
+    AKO_RMS_CASE(T, RES, 1, 64, 16) \
     AKO_RMS_CASE(T, RES, 1, 128, 1) \
     AKO_RMS_CASE(T, RES, 1, 128, 2) \
     AKO_RMS_CASE(T, RES, 1, 128, 4) \
     AKO_RMS_CASE(T, RES, 1, 128, 8) \
+    AKO_RMS_CASE(T, RES, 1, 128, 16) \
     AKO_RMS_CASE(T, RES, 1, 256, 1) \
     AKO_RMS_CASE(T, RES, 1, 256, 2) \
     AKO_RMS_CASE(T, RES, 1, 256, 4) \
