@@ -1,14 +1,15 @@
 """Per-cell sweep of BASELINE configs 1-4 on one GPU, with competitors.
 
 For every op / shape / dtype cell it reports the device time of the sm_100a
-kernel (median over launches, L2 flushed by a 2x-L2 read before each), the
-achieved GB/s on the algorithmic bytes, and the fraction of the measured HBM
-copy bandwidth. Competitors are timed the same way: the unfused reference
+kernel from a cold L2 (differential timing: n x (2x-L2 read, call) minus n
+reads, over n; event steps of ~2 us average out and each call is charged
+the write-back of its outputs), the achieved GB/s on the algorithmic bytes,
+and the fraction of the measured HBM copy bandwidth. Competitors are timed the same way: the unfused reference
 (eager), its ``torch.compile`` form, ``F.rms_norm`` and, when the reference
 package is importable (``--reference-path``), AKO's own Triton kernels. Decode
 cells (one token per sequence) add the wall-clock latency per call of
-back-to-back calls, which is what a decode loop pays, and the replay time of
-a CUDA graph holding one call. Each cell is also checked against the eager
+back-to-back calls, which is what a decode loop pays, and the device time per
+call of 20 calls captured in one CUDA graph. Each cell is also checked against the eager
 reference with AKO's error budget.
 
     python -m ako_b200.benchmark.sweep --out gpurun_out/sweep.json [--configs 1,2,3,4]
@@ -27,10 +28,10 @@ from typing import Any, Callable
 import torch
 
 from ako_b200 import kernels
+from ako_b200.benchmark.timing import Flusher, cold_us
 from ako_b200.dispatch import references as refs
 from ako_b200.dispatch.numerical import error_budget, error_in_ulps, max_abs_error_any
 
-L2_FLUSH_BYTES = 2 * 126 * 1024 * 1024
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 
 
@@ -124,18 +125,9 @@ def make_inputs(cell: dict[str, Any], dev: torch.device, tables: dict) -> tuple[
     return (rnd(m, f, sd=2.0), rnd(m, f, sd=2.0)), {}, 3 * m * f * b
 
 
-def device_us(fn: Callable, args: tuple, n: int, flush: torch.Tensor) -> float:
-    sink = torch.empty((), dtype=torch.int64, device=flush.device)
-    for _ in range(3):
-        fn(*args)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-    for s, e in evs:
-        torch.sum(flush.view(torch.int64), dim=0, out=sink)
-        s.record()
-        fn(*args)
-        e.record()
-    torch.cuda.synchronize()
-    return statistics.median(s.elapsed_time(e) * 1e3 for s, e in evs)
+def device_us(fn: Callable, args: tuple, n: int, flush: Flusher) -> float:
+    """Cold-L2 device time of one call (differential timing, see ako_b200.benchmark.timing)."""
+    return cold_us(lambda: fn(*args), flush, n=n)
 
 
 def wall_us(fn: Callable, args: tuple, batches: int = 15, inner: int = 50) -> float:
@@ -153,8 +145,9 @@ def wall_us(fn: Callable, args: tuple, batches: int = 15, inner: int = 50) -> fl
     return statistics.median(samples)
 
 
-def graph_us(fn: Callable, args: tuple, inner: int = 100) -> float | None:
-    """Device time per replay of a CUDA graph holding one call; None if capture fails."""
+def graph_us(fn: Callable, args: tuple, calls: int = 20, replays: int = 40) -> float | None:
+    """Device time per call of ``calls`` calls captured in one CUDA graph (best
+    of three timed runs of ``replays`` replays); None if capture fails."""
     try:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -164,17 +157,21 @@ def graph_us(fn: Callable, args: tuple, inner: int = 100) -> float | None:
         torch.cuda.current_stream().wait_stream(side)
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
-            fn(*args)
+            for _ in range(calls):
+                fn(*args)
+        for _ in range(2):
+            gr.replay()
+        torch.cuda.synchronize()
+        best = float("inf")
         for _ in range(3):
-            gr.replay()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(inner):
-            gr.replay()
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e) * 1e3 / inner
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(replays):
+                gr.replay()
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e) * 1e3 / (replays * calls))
+        return round(best, 3)
     except Exception:  # noqa: BLE001 - a candidate that cannot be captured is reported as such
         return None
 
@@ -184,7 +181,7 @@ def main() -> None:
     ap.add_argument("--configs", default="1,2,3,4")
     ap.add_argument("--competitors", default="eager,compile,triton,native")
     ap.add_argument("--reference-path", default="baseline/_ref")
-    ap.add_argument("--launches", type=int, default=15)
+    ap.add_argument("--launches", type=int, default=20)
     ap.add_argument("--peak-gbs", type=float, default=None)
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
@@ -200,7 +197,7 @@ def main() -> None:
     ref_pkg = _reference_package(args.reference_path)
     comps = ref_pkg or _own_competitors()
     wanted = set(args.competitors.split(","))
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = Flusher(dev)
     tables = {128: refs.build_rope_tables(8192, 128, device=dev)}
     results = []
     for cell in cells({int(c) for c in args.configs.split(",")}):
@@ -223,7 +220,7 @@ def main() -> None:
             candidates["native"] = refs.rmsnorm_torch_native
         for name, fn in candidates.items():
             try:
-                row[f"{name}_us"] = round(device_us(fn, inputs, max(5, args.launches // 3), flush), 3)
+                row[f"{name}_us"] = round(device_us(fn, inputs, max(5, args.launches // 2), flush), 3)
             except Exception as exc:  # noqa: BLE001 - a competitor that cannot run this cell
                 row[f"{name}_us"] = None
                 row[f"{name}_error"] = f"{type(exc).__name__}: {str(exc)[:120]}"

@@ -19,8 +19,8 @@ L2, so back-to-back steps need no flush).
   ncu summary of this workload.
 * ``cpu_baseline``: the C oracle (a restatement of AKO's unfused reference,
   all host threads) on a bounded row sample of the same workload, rank 0, N=1.
-* ``ops``: the other ops at their largest BASELINE cell (N=1), per-launch
-  device time with the L2 flushed before each launch.
+* ``ops``: the other ops at their largest BASELINE cell (N=1), device time
+  per call from a cold L2 (differential timing).
 
 Multi-GPU (torchrun): every rank owns its own row shard (weak scaling); no
 collective touches the data path, only the max of the timings.
@@ -204,34 +204,18 @@ def ncu_traffic(workload: str) -> int | None:
 
 
 # ---------------------------------------------------------------- extras
-def per_launch_us(fn, n: int, flush: torch.Tensor) -> list[float]:
-    """Device time of each launch, L2 flushed before each by reading twice its
-    size (a read leaves clean lines, so the timed kernel pays no write-backs)."""
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-    sink = torch.empty((), dtype=torch.int64, device=flush.device)
-    for s, e in evs:
-        torch.sum(flush.view(torch.int64), dim=0, out=sink)
-        s.record()
-        fn()
-        e.record()
-    torch.cuda.synchronize()
-    return [s.elapsed_time(e) * 1000.0 for s, e in evs]
-
-
 def run_ops(device: torch.device, peak: float) -> dict:
-    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+    from ako_b200.benchmark.timing import Flusher, cold_us
+
+    flush = Flusher(device)
     out = {}
     for name in OPS_EXTRA:
         wl = Workload(name, device, seed=1)
-        for _ in range(3):
-            wl.step()
-        us = per_launch_us(wl.step, 10, flush)
-        mean_us = statistics.mean(us)
-        med_us = statistics.median(us)
-        gbs = wl.bytes / (med_us * 1e-6) / 1e9
+        us = cold_us(wl.step, flush, n=10, blocks=3)
+        gbs = wl.bytes / (us * 1e-6) / 1e9
         out[name] = {"op": wl.op, **wl.desc, "dtype": str(wl.dtype).replace("torch.", ""),
-                     "bytes": wl.bytes, "us_mean": round(mean_us, 2), "us_median": round(med_us, 2),
-                     "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+                     "bytes": wl.bytes, "us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "timing": "cold L2, differential (10 x (2xL2 read, call) - 10 x read) / 10"}
         del wl
         torch.cuda.empty_cache()
     return out
