@@ -24,6 +24,12 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
     return __float2bfloat16_rn(v);
 }
 
+// The C ABI's dtype code of a storage type.
+template <typename T>
+constexpr int dtype_code() {
+    return std::is_same_v<T, float> ? AKO_B200_F32 : (std::is_same_v<T, __half> ? AKO_B200_F16 : AKO_B200_BF16);
+}
+
 // N elements of T moved as one access (16 bytes when N * sizeof(T) == 16).
 template <typename T, int N>
 struct alignas(sizeof(T) * N) Packed {

@@ -38,7 +38,8 @@ bool use_staged(const RmsArgs& a, int es) {
 //    one CTA's registers hold (8192 vectors) are split over a cluster of 8.
 //  * Few rows (decode): latency, not bandwidth, decides. One vector per
 //    thread (twice the threads) up to 512-vector rows; 2048-vector rows split
-//    over a cluster of 4 CTAs so a row's loads come from 4 SMs at once.
+//    over a cluster of 4 CTAs and 4096-vector rows over 4 or 8, so a row's
+//    loads come from several SMs at once.
 bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
     const Shape& o = g_override;
     if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
@@ -53,6 +54,10 @@ bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
     }
     if (nvec > 1024 && nvec <= 2048 && nvec % 4 == 0 && rows <= 64) {
         *out = rows <= 32 ? Shape{4, 512, 1} : Shape{4, 256, 2};
+        return true;
+    }
+    if (nvec > 2048 && nvec <= 4096 && nvec % 8 == 0 && rows <= 64) {
+        *out = rows <= 8 ? Shape{8, 256, 2} : Shape{4, 512, 2};
         return true;
     }
     static const Shape table[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
@@ -73,7 +78,7 @@ bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
 template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok && use_staged(a, sizeof(T))) {
-        const int dtype = sizeof(T) == 4 ? AKO_B200_F32 : (std::is_same_v<T, __half> ? AKO_B200_F16 : AKO_B200_BF16);
+        const int dtype = dtype_code<T>();
         const int stages = g_stages > 0 ? g_stages : 4;
         const int ctas = g_ctas_per_sm > 0 ? g_ctas_per_sm : 2;
         const int rc = launch_rms_staged(a, dtype, RES, stages, ctas, st);

@@ -46,11 +46,25 @@ struct RmsShape {
     static constexpr int kRowsPerCta = kThreads / TPR;
 };
 
+// Most vectors per thread for which the weight is held in registers.
+constexpr int WEIGHT_NV = 2;
+
+// CTAs per SM the register allocation must leave room for (the second
+// launch bound; 0 leaves it out). 512-thread CTAs with the weight in
+// registers take 46-48 registers a thread unbounded, which fits two per SM;
+// at 40 three fit, and rows of 1024 bf16 vectors run 5-7% faster (measured
+// on B200). Other shapes are faster unbounded: an explicit bound of 1
+// changes their code even where it does not bind.
+template <int TPR, int NV>
+constexpr int rms_min_ctas() {
+    return (RmsShape<TPR>::kThreads == 512 && NV <= WEIGHT_NV) ? 3 : 0;
+}
+
 // CLUSTER > 1: a row is split into CLUSTER equal slices, one per CTA of a
 // thread-block cluster; CTA partial sums are exchanged through distributed
 // shared memory, so each CTA holds only H / CLUSTER elements in registers.
 template <typename T, int TPR, int NV, bool RES, int CLUSTER>
-__global__ void __launch_bounds__(RmsShape<TPR>::kThreads)
+__global__ void __launch_bounds__(RmsShape<TPR>::kThreads, rms_min_ctas<TPR, NV>())
 rms_rows_kernel(const RmsArgs a) {
     constexpr int VEC = 16 / sizeof(T);
     constexpr int THREADS = RmsShape<TPR>::kThreads;
@@ -77,12 +91,34 @@ rms_rows_kernel(const RmsArgs a) {
         const int col = (j * TPR + lane) * VEC;
         if (col < width) v[j] = ld_stream<T, VEC>(xr + col);
     }
-    // The weight is needed only after the reduction; start its fetch now so
-    // it is not a second memory round trip on the row's critical path.
+    // The weight is needed only after the reduction. Fetching it there puts a
+    // second memory round trip on every row's critical path (measured: up to
+    // 20% of the kernel on 8192 x 2048 bf16 rows). When it has the row's dtype
+    // (the usual case) it is loaded now, next to the row, and held packed like
+    // the row (4 registers per vector); other weight dtypes, and shapes with
+    // more than WEIGHT_NV vectors per thread, prefetch it to L1 instead.
+    constexpr bool kWeightRegs = NV <= WEIGHT_NV;
+    P wv[kWeightRegs ? NV : 1];
+    bool w_regs = false;
+    if constexpr (kWeightRegs) {
+        w_regs = a.wdtype == dtype_code<T>();
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int col = (j * TPR + lane) * VEC;
-        if (col < width) prefetch_weight(a.w, a.wdtype, c0 + col);
+        for (int j = 0; j < NV; ++j) {
+            const int col = (j * TPR + lane) * VEC;
+            if (col < width) {
+                if (w_regs) {
+                    wv[j] = ld_cached<T, VEC>(static_cast<const T*>(a.w) + c0 + col);
+                } else {
+                    prefetch_weight(a.w, a.wdtype, c0 + col);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int col = (j * TPR + lane) * VEC;
+            if (col < width) prefetch_weight(a.w, a.wdtype, c0 + col);
+        }
     }
 
     if constexpr (RES) {
@@ -152,13 +188,22 @@ rms_rows_kernel(const RmsArgs a) {
     for (int j = 0; j < NV; ++j) {
         const int col = (j * TPR + lane) * VEC;
         if (col < width) {
-            float w[VEC];
-            load_weight_vec<VEC>(a.w, a.wdtype, c0 + col, w);
             P o;
+            if (kWeightRegs && w_regs) {
 #pragma unroll
-            for (int e = 0; e < VEC; e += 2) {
-                const float2 f = get2<T, VEC>(v[j], e);
-                put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w[e]), __fmul_rn(__fmul_rn(f.y, inv), w[e + 1]));
+                for (int e = 0; e < VEC; e += 2) {
+                    const float2 f = get2<T, VEC>(v[j], e);
+                    const float2 w = get2<T, VEC>(wv[kWeightRegs ? j : 0], e);
+                    put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w.x), __fmul_rn(__fmul_rn(f.y, inv), w.y));
+                }
+            } else {
+                float w[VEC];
+                load_weight_vec<VEC>(a.w, a.wdtype, c0 + col, w);
+#pragma unroll
+                for (int e = 0; e < VEC; e += 2) {
+                    const float2 f = get2<T, VEC>(v[j], e);
+                    put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w[e]), __fmul_rn(__fmul_rn(f.y, inv), w[e + 1]));
+                }
             }
             st_global<T, VEC>(yr + col, o);
         }

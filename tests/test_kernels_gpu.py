@@ -137,6 +137,13 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
                 assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"shape {cl}x{tpr}x{nv} h={h}")
                 y1 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-6)
                 assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1), dtype, "rmsnorm", f"shape {cl}x{tpr}x{nv}")
+                if dtype == O.BF16:
+                    # a weight of another dtype takes the kernel's second weight path
+                    w32 = normal(rng, (h,), 1, 0.1, O.F32)
+                    y2 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w32, O.F32, cuda_device),
+                                                    1e-6)
+                    assert_parity(C.rmsnorm(x, w32, 1e-6, dtype, O.F32), to_numpy(y2), dtype, "rmsnorm",
+                                  f"fp32 weight, shape {cl}x{tpr}x{nv}")
     finally:
         lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
 
