@@ -1,6 +1,7 @@
 // C-ABI entry points for RMSNorm and fused residual-add RMSNorm: argument
 // checks, choice of launch shape, dispatch on dtype.
 #include <climits>
+#include <cmath>
 
 #include "rmsnorm.cuh"
 
@@ -31,22 +32,29 @@ bool use_staged(const RmsArgs& a, int es) {
 // Launch shape for `rows` rows of `nvec` 16-byte vectors, from sweeps of
 // every built shape on B200 (bf16, fp16, fp32; 2048..16384 wide; 1 to 32768
 // rows; device time per call with the L2 cold, and inside CUDA graphs).
-//  * Many rows: one CTA per row with two vectors per thread up to 512
-//    threads (1024-vector rows): registers stay low enough for several CTAs
-//    per SM, so loads of the next rows are in flight while a row reduces.
-//    Wider rows keep 512-1024 threads with 4 vectors each; rows wider than
-//    one CTA's registers hold (8192 vectors) are split over a cluster of 8.
+//  * Many rows: one CTA per row. The fused residual form moves two rows in
+//    and two out, so two vectors per thread up to 512 threads (1024-vector
+//    rows) keep enough loads in flight; wider rows keep 512-1024 threads with
+//    4 vectors each. Plain RMSNorm moves half as much per row and wants twice
+//    the vectors per thread with fewer threads (64-512 threads x 4, 512 x 8
+//    for 4096-vector rows), which also halves the per-warp fixed work. Rows
+//    wider than one CTA's registers hold (8192 vectors) are split over a
+//    cluster of 8.
 //  * Few rows (decode): latency, not bandwidth, decides. One vector per
 //    thread (twice the threads) up to 512-vector rows; 2048-vector rows split
 //    over a cluster of 4 CTAs and 4096-vector rows over 4 or 8, so a row's
 //    loads come from several SMs at once.
-bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
+bool pick_shape(int64_t nvec, int64_t rows, bool residual, Shape* out) {
     const Shape& o = g_override;
     if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
         *out = o;
         return true;
     }
     if (rows <= 512 && nvec > 32 && nvec <= 512) {
+        if (!residual && nvec > 256 && rows > 64) {
+            *out = Shape{1, 256, 2};
+            return true;
+        }
         int tpr = 64;
         while (tpr < nvec) tpr *= 2;
         *out = Shape{1, tpr, 1};
@@ -60,9 +68,11 @@ bool pick_shape(int64_t nvec, int64_t rows, Shape* out) {
         *out = rows <= 8 ? Shape{8, 256, 2} : Shape{4, 512, 2};
         return true;
     }
-    static const Shape table[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
+    static const Shape fused[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
                                   {1, 256, 2}, {1, 512, 2}, {1, 512, 4}, {1, 1024, 4}};
-    for (const Shape& s : table) {
+    static const Shape plain[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 64, 4},
+                                  {1, 128, 4}, {1, 256, 4}, {1, 512, 4}, {1, 512, 8}};
+    for (const Shape& s : residual ? fused : plain) {
         if (static_cast<int64_t>(s.tpr) * s.nv >= nvec) {
             *out = s;
             return true;
@@ -87,7 +97,7 @@ int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok) {
         constexpr int VEC = 16 / sizeof(T);
         Shape s;
-        if (pick_shape(a.h / VEC, a.rows, &s)) {
+        if (pick_shape(a.h / VEC, a.rows, RES, &s)) {
             const int rc = launch_rms_rows<T, RES>(a, s.cluster, s.tpr, s.nv, st);
             if (rc >= 0) return rc;
         }
@@ -103,6 +113,11 @@ int dispatch(const RmsArgs& a, int dtype, bool vector_ok, cudaStream_t st) {
         case AKO_B200_BF16: return run<__nv_bfloat16, RES>(a, vector_ok, st);
         default: return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
     }
+}
+
+// 1 / h for a power of two h (exact in fp32 for h <= 2^126), else 0.
+float pow2_reciprocal(int64_t h) {
+    return (h & (h - 1)) == 0 ? std::ldexp(1.0f, -std::ilogb(static_cast<double>(h))) : 0.0f;
 }
 
 int check_common(const char* op, int64_t rows, int64_t h, int dtype, int wdtype) {
@@ -147,7 +162,7 @@ extern "C" int ako_b200_rmsnorm(const void* x, int64_t x_row_stride, const void*
     if (weight == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: weight is a null pointer", op);
 
     RmsArgs a{x, x_row_stride, nullptr, 0, weight, weight_dtype, y, y_row_stride, nullptr, 0,
-              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps)};
+              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps), pow2_reciprocal(hidden_dim)};
     const int es = dtype_size(dtype);
     const bool vector_ok = (hidden_dim * es) % 16 == 0 && aligned16(x) && aligned16(y) && aligned16(weight) &&
                            stride_ok16(x_row_stride, n_rows, es) && stride_ok16(y_row_stride, n_rows, es);
@@ -172,7 +187,7 @@ extern "C" int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride, co
 
     RmsArgs a{x,      x_row_stride,  residual, residual_row_stride, weight, weight_dtype,
               y,      y_row_stride,  residual_out, residual_out_row_stride,
-              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps)};
+              n_rows, static_cast<int>(hidden_dim), static_cast<float>(eps), pow2_reciprocal(hidden_dim)};
     const int es = dtype_size(dtype);
     const bool vector_ok = (hidden_dim * es) % 16 == 0 && aligned16(x) && aligned16(residual) && aligned16(y) &&
                            aligned16(residual_out) && aligned16(weight) && stride_ok16(x_row_stride, n_rows, es) &&

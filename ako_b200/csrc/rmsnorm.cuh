@@ -38,7 +38,17 @@ struct RmsArgs {
     int64_t rows;
     int h;
     float eps;
+    float inv_h;  // 1 / h when h is a power of two (then exact), else 0
 };
+
+// 1 / sqrt(sum / h + eps) with the reference's roundings: the mean is one
+// IEEE quotient (a product with inv_h when h is a power of two: scaling by a
+// power of two rounds the same real number), then an IEEE square root and
+// the correctly rounded reciprocal, which is the IEEE quotient 1 / s.
+__device__ __forceinline__ float rms_inv(float total, const RmsArgs& a) {
+    const float mean = a.inv_h != 0.0f ? __fmul_rn(total, a.inv_h) : __fdiv_rn(total, static_cast<float>(a.h));
+    return __frcp_rn(__fsqrt_rn(__fadd_rn(mean, a.eps)));
+}
 
 template <int TPR>
 struct RmsShape {
@@ -46,8 +56,12 @@ struct RmsShape {
     static constexpr int kRowsPerCta = kThreads / TPR;
 };
 
-// Most vectors per thread for which the weight is held in registers.
+// The weight is held in registers (4 per vector) by shapes with at most
+// WEIGHT_NV vectors per thread, or at most WEIGHT_CTA_VECTORS vectors per
+// CTA (few threads, many vectors each: the register file is not what bounds
+// their occupancy).
 constexpr int WEIGHT_NV = 2;
+constexpr int WEIGHT_CTA_VECTORS = 1024;
 
 // CTAs per SM the register allocation must leave room for (the second
 // launch bound; 0 leaves it out). 512-thread CTAs with the weight in
@@ -95,9 +109,9 @@ rms_rows_kernel(const RmsArgs a) {
     // second memory round trip on every row's critical path (measured: up to
     // 20% of the kernel on 8192 x 2048 bf16 rows). When it has the row's dtype
     // (the usual case) it is loaded now, next to the row, and held packed like
-    // the row (4 registers per vector); other weight dtypes, and shapes with
-    // more than WEIGHT_NV vectors per thread, prefetch it to L1 instead.
-    constexpr bool kWeightRegs = NV <= WEIGHT_NV;
+    // the row (4 registers per vector); other weight dtypes, and shapes whose
+    // registers are better spent on occupancy, prefetch it to L1 instead.
+    constexpr bool kWeightRegs = NV <= WEIGHT_NV || THREADS * NV <= WEIGHT_CTA_VECTORS;
     P wv[kWeightRegs ? NV : 1];
     bool w_regs = false;
     if constexpr (kWeightRegs) {
@@ -180,8 +194,7 @@ rms_rows_kernel(const RmsArgs a) {
         total = tree_sum<CLUSTER>(parts);
         cluster_arrive();
     }
-    const float mean = __fdiv_rn(total, static_cast<float>(a.h));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    const float inv = rms_inv(total, a);
 
     T* yr = static_cast<T*>(a.y) + row * a.sy + c0;
 #pragma unroll
@@ -234,8 +247,7 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
         acc += static_cast<double>(__fmul_rn(f, f));
     }
     const float total = block_sum<kGenericThreads>(static_cast<float>(acc), scratch);
-    const float mean = __fdiv_rn(total, static_cast<float>(a.h));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    const float inv = rms_inv(total, a);
 
     T* yr = static_cast<T*>(a.y) + row * a.sy;
     for (int col = threadIdx.x; col < a.h; col += kGenericThreads) {

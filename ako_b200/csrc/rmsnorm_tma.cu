@@ -143,8 +143,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
 #pragma unroll
         for (int i = 0; i < WARPS; ++i) parts[i] = sc[i];
         const float total = tree_sum<WARPS>(parts);
-        const float mean = __fdiv_rn(total, static_cast<float>(h));
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        const float inv = rms_inv(total, a);
         T* yr = static_cast<T*>(a.y) + row * a.sy;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {

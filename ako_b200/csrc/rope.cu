@@ -108,10 +108,10 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
                 const T* xp;
                 head_rows<T>(a, h0 + j, b, s, xp, yrow[j]);
                 if constexpr (INTERLEAVED) {
-                    lo[j] = ld_stream<T, E>(xp + 2 * p0);
+                    lo[j] = ld_stream_no_l1<T, E>(xp + 2 * p0);
                 } else {
-                    lo[j] = ld_stream<T, E>(xp + p0);
-                    hi[j] = ld_stream<T, E>(xp + a.half + p0);
+                    lo[j] = ld_stream_no_l1<T, E>(xp + p0);
+                    hi[j] = ld_stream_no_l1<T, E>(xp + a.half + p0);
                 }
             }
         }
