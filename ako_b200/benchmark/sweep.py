@@ -1,4 +1,4 @@
-"""Per-cell sweep of BASELINE configs 1-4 on one GPU, with competitors.
+"""Per-cell sweep of the four benchmark configurations on one GPU, with competitors.
 
 For every op / shape / dtype cell it reports the device time of the sm_100a
 kernel from a cold L2 (differential timing: n x (2x-L2 read, call) minus n
@@ -12,13 +12,17 @@ back-to-back calls, which is what a decode loop pays, and the device time per
 call of 20 calls captured in one CUDA graph. Each cell is also checked against the eager
 reference with AKO's error budget.
 
-    python -m ako_b200.benchmark.sweep --out gpurun_out/sweep.json [--configs 1,2,3,4]
+    python -m ako_b200.benchmark.sweep --out sweep.json [--configs 1,2,3,4]
+    python -m ako_b200.benchmark.sweep --report sweep.json > sweep.md
+
+``--report`` renders a sweep JSON as markdown tables with summary counts.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import statistics
 import sys
 import time
@@ -125,9 +129,9 @@ def make_inputs(cell: dict[str, Any], dev: torch.device, tables: dict) -> tuple[
     return (rnd(m, f, sd=2.0), rnd(m, f, sd=2.0)), {}, 3 * m * f * b
 
 
-def device_us(fn: Callable, args: tuple, n: int, flush: Flusher) -> float:
+def device_us(fn: Callable, args: tuple, n: int, flush: Flusher, blocks: int) -> float:
     """Cold-L2 device time of one call (differential timing, see ako_b200.benchmark.timing)."""
-    return cold_us(lambda: fn(*args), flush, n=n)
+    return cold_us(lambda: fn(*args), flush, n=n, blocks=blocks)
 
 
 def wall_us(fn: Callable, args: tuple, batches: int = 15, inner: int = 50) -> float:
@@ -176,15 +180,137 @@ def graph_us(fn: Callable, args: tuple, calls: int = 20, replays: int = 40) -> f
         return None
 
 
+# ------------------------------------------------------------------ report
+TITLES = {
+    1: "Config 1 — RMSNorm fp32 [4,512,4096] (2048 rows x 4096)",
+    2: "Config 2 — fused residual-add RMSNorm",
+    3: "Config 3 — RoPE neox, D=128, fp32 [8192,64] table sliced (S=1 at position 2047)",
+    4: "Config 4 — SwiGLU, separate [M,F] or packed [M,2F]",
+}
+COMPETITORS = ("triton", "compile", "eager")
+
+
+def cell_label(c: dict[str, Any]) -> str:
+    if c["op"] in ("rmsnorm", "rmsnorm_residual"):
+        return f"M{c['rows']} H{c['hidden']}"
+    if c["op"] == "rope":
+        return f"B{c['batch']} S{c['seq']} {c['tensor']}({c['heads']}h)"
+    return f"M{c['rows']} F{c['hidden']}" + (" packed" if c.get("packed") else "")
+
+
+def _fmt(v: float | None, nd: int = 3) -> str:
+    if v is None:
+        return "-"
+    return f"{v:.{nd}g}" if v < 100 else f"{v:.0f}" if v >= 1000 else f"{v:.1f}"
+
+
+def _ratio(c: dict[str, Any], name: str, key: str = "us") -> float | None:
+    theirs, ours = c.get(f"{name}_{key}"), c.get(f"ours_{key}")
+    return theirs / ours if theirs and ours else None
+
+
+def _geomean(xs: list[float]) -> float:
+    return math.exp(sum(math.log(x) for x in xs) / len(xs)) if xs else float("nan")
+
+
+def report(summary: dict[str, Any]) -> str:
+    """Markdown tables and summary counts of one sweep JSON."""
+    cells = summary["cells"]
+    peak = summary["peak_gbs"]
+    n, blocks = summary.get("launches", 20), summary.get("blocks", 5)
+    out = ["# Per-cell sweep of benchmark configurations 1-4 on one B200", "",
+           "    python -m ako_b200.benchmark.sweep --out sweep.json",
+           "    python -m ako_b200.benchmark.sweep --report sweep.json", "",
+           "Columns:",
+           f"- `us`: device time of one call from a cold L2, differential: n x (read of 2 x the L2 size, call)",
+           f"  minus n reads, over n, with n = {n}; median of {blocks} such blocks. The read evicts the previous",
+           "  call's outputs, so each call is charged the write-back of what it wrote.",
+           f"- `GB/s`: algorithmic bytes over `us`. `frac`: that over the measured {peak} GB/s copy bandwidth.",
+           "- Competitors are timed the same way:",
+           "  - `triton`: AKO's own Triton kernels, JIT-compiled for sm_100 on this GPU;",
+           "  - `compile`: AKO's `torch.compile` form of the reference;",
+           "  - `eager`: AKO's unfused reference.",
+           "  All three come from the reference package installed offline into `baseline/_ref`."
+           if summary.get("reference_package") else
+           "  The reference package was not importable: `compile` and `eager` are this package's restatements.",
+           "- `x` columns: competitor time over ours (above 1: ours is faster).",
+           "- `ulps`: AKO's `error_in_ulps` of our output against its eager reference.", ""]
+    fails = [c for c in cells if not c["parity"]]
+    out.append(f"All {len(cells)} cells pass AKO's error budget." if not fails else
+               f"{len(fails)} of {len(cells)} cells fail AKO's error budget: " +
+               ", ".join(f"{c['op']} {c['dtype']} {cell_label(c)}" for c in fails) + ".")
+    maxu = {}
+    for c in cells:
+        maxu[c["op"]] = max(maxu.get(c["op"], 0.0), c["ulps"])
+    out.append("Max reported ulps: " + ", ".join(f"{op} {u:g}" + (" (bit-exact)" if u == 0 else "")
+                                                 for op, u in maxu.items()) + ".")
+    out.append("")
+    out.append("Throughput cells (not decode), ours against each competitor: cells where ours is at or below "
+               "its time, and the geometric mean of its time over ours.")
+    out.append("")
+    out.append("| op | cells | " + " | ".join(f"vs {n}" for n in COMPETITORS) + " |")
+    out.append("|---|---:|" + "---|" * len(COMPETITORS))
+    for op in dict.fromkeys(c["op"] for c in cells):
+        cs = [c for c in cells if c["op"] == op and not c.get("decode")]
+        if not cs:
+            continue
+        parts = []
+        for n in COMPETITORS:
+            rs = [r for r in (_ratio(c, n) for c in cs) if r]
+            parts.append(f"{sum(r >= 1.0 for r in rs)}/{len(rs)}, x{_geomean(rs):.2f}" if rs else "-")
+        out.append(f"| {op} | {len(cs)} | " + " | ".join(parts) + " |")
+    out.append("")
+    for cfg in sorted({c["config"] for c in cells}):
+        out += [f"## {TITLES[cfg]}", "",
+                "| dtype | cell | us | GB/s | frac | " + " | ".join(f"x {n}" for n in COMPETITORS) + " | ulps |",
+                "|---|---|---:|---:|---:|" + "---:|" * len(COMPETITORS) + "---:|"]
+        for c in cells:
+            if c["config"] != cfg:
+                continue
+            xs = " | ".join(f"{r:.2f}" if (r := _ratio(c, n)) else "-" for n in COMPETITORS)
+            out.append(f"| {c['dtype']} | {cell_label(c)} | {_fmt(c['ours_us'])} | {c['ours_gbs']:.0f} | "
+                       f"{c['frac']:.3f} | {xs} | {c['ulps']:g} |")
+        out.append("")
+    dec = [c for c in cells if c.get("decode")]
+    if dec:
+        out += ["## Decode cells: latency a decode loop pays", "",
+                "- `wall`: wall clock per call of back-to-back calls from Python (p50 of 15 batches of 50). This is",
+                "  what AKO's selector compares (`latency_p50_ms`).",
+                "- `graph`: device time per call of 20 calls captured in one CUDA graph (best of 3 timed runs of",
+                "  40 replays).", "",
+                "| op | dtype | cell | " + " | ".join(f"wall {n}" for n in ("ours", *COMPETITORS)) + " | " +
+                " | ".join(f"graph {n}" for n in ("ours", *COMPETITORS)) + " |",
+                "|---|---|---|" + "---:|" * (2 * (1 + len(COMPETITORS)))]
+        for c in dec:
+            walls = " | ".join(_fmt(c.get(f"{n}_wall_us")) for n in ("ours", *COMPETITORS))
+            graphs = " | ".join(_fmt(c.get(f"{n}_graph_us")) for n in ("ours", *COMPETITORS))
+            out.append(f"| {c['op']} | {c['dtype']} | {cell_label(c)} | {walls} | {graphs} |")
+        out.append("")
+        for n in COMPETITORS:
+            w = [r for r in (_ratio(c, n, "wall_us") for c in dec) if r]
+            g = [r for r in (_ratio(c, n, "graph_us") for c in dec) if r]
+            if w or g:
+                out.append(f"- vs {n}: wall clock, ours faster on {sum(r > 1 for r in w)} of {len(w)} cells "
+                           f"(x{_geomean(w):.2f}); in a graph, ours at or below on {sum(r >= 1 for r in g)} of "
+                           f"{len(g)} (x{_geomean(g):.2f}).")
+        out.append("")
+    return "\n".join(out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--report", default=None, help="render this sweep JSON as markdown and exit")
     ap.add_argument("--configs", default="1,2,3,4")
     ap.add_argument("--competitors", default="eager,compile,triton,native")
     ap.add_argument("--reference-path", default="baseline/_ref")
-    ap.add_argument("--launches", type=int, default=20)
+    ap.add_argument("--launches", type=int, default=20, help="calls per timed block")
+    ap.add_argument("--blocks", type=int, default=7, help="timed blocks per cell (median)")
     ap.add_argument("--peak-gbs", type=float, default=None)
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
+    if args.report:
+        print(report(json.loads(Path(args.report).read_text())))
+        return
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -211,7 +337,7 @@ def main() -> None:
         row["budget"] = error_budget(ref)
         row["ulps"] = round(error_in_ulps(ref, out), 3)
         row["parity"] = row["max_error"] <= row["budget"]
-        us = device_us(ours, inputs, args.launches, flush)
+        us = device_us(ours, inputs, args.launches, flush, args.blocks)
         row["ours_us"] = round(us, 3)
         row["ours_gbs"] = round(nbytes / us / 1e3, 1)
         row["frac"] = round(nbytes / us / 1e3 / peak, 4)
@@ -220,7 +346,7 @@ def main() -> None:
             candidates["native"] = refs.rmsnorm_torch_native
         for name, fn in candidates.items():
             try:
-                row[f"{name}_us"] = round(device_us(fn, inputs, max(5, args.launches // 2), flush), 3)
+                row[f"{name}_us"] = round(device_us(fn, inputs, args.launches, flush, args.blocks), 3)
             except Exception as exc:  # noqa: BLE001 - a competitor that cannot run this cell
                 row[f"{name}_us"] = None
                 row[f"{name}_error"] = f"{type(exc).__name__}: {str(exc)[:120]}"
@@ -234,7 +360,8 @@ def main() -> None:
         results.append(row)
         print(json.dumps(row), flush=True)
         del inputs, out, ref
-    summary = {"peak_gbs": peak, "reference_package": ref_pkg is not None,
+    summary = {"peak_gbs": peak, "reference_package": ref_pkg is not None, "launches": args.launches,
+               "blocks": args.blocks,
                "gpu": torch.cuda.get_device_name(dev), "cells": results}
     if args.out:
         Path(args.out).write_text(json.dumps(summary, indent=1))

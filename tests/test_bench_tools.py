@@ -1,0 +1,79 @@
+"""CPU tests of the measurement tools: the reference arm of ``bench.py`` (the
+C oracle on the host cores) keeps the JSON line contract, ``bench.py``
+refuses fewer than 3 warm-up steps, and the sweep report renders its tables
+and counts from a sweep JSON."""
+
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+from ako_b200.benchmark.sweep import cell_label, report
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _bench(*args: str, timeout: int = 240) -> subprocess.CompletedProcess:
+    return subprocess.run([sys.executable, "bench.py", *args], cwd=REPO, capture_output=True, text=True,
+                          timeout=timeout)
+
+
+def test_reference_arm_json_line() -> None:
+    proc = _bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, proc.stdout
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference"
+    assert rec["metric"] == "achieved HBM GB/s" and rec["unit"] == "GB/s" and rec["higher_is_better"] is True
+    assert rec["value"] > 0 and rec["steps"] == 1 and rec["warmup"] == 3 and rec["n_gpus"] == 1
+    assert rec["config"]["workload"] == "rmsnorm_residual_bf16_32768x16384"
+    cb = rec["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == rec["value"] and cb["sample"]
+    assert rec["e2e"] == {"value": rec["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_bench_refuses_short_warmup() -> None:
+    proc = _bench("--impl", "reference", "--steps", "1", "--warmup", "2", timeout=60)
+    assert proc.returncode == 2
+    assert "--warmup must be >= 3" in proc.stderr
+
+
+def _cell(op: str, **kw) -> dict:
+    base = {"config": {"rmsnorm": 1, "rmsnorm_residual": 2, "rope": 3, "swiglu": 4}[op], "op": op, "dtype": "bf16",
+            "bytes": 1 << 20, "max_error": 0.0, "budget": 0.1, "ulps": 0.5, "parity": True, "ours_us": 10.0,
+            "ours_gbs": 100.0, "frac": 0.5, "triton_us": 12.0, "compile_us": 20.0, "eager_us": 40.0}
+    base.update(kw)
+    return base
+
+
+def test_sweep_report_tables_and_counts() -> None:
+    cells = [
+        _cell("rmsnorm", dtype="fp32", rows=2048, hidden=4096, triton_us=9.0, ulps=2.0),
+        _cell("rmsnorm_residual", rows=8192, hidden=4096),
+        _cell("rmsnorm_residual", rows=1, hidden=4096, decode=True, ours_wall_us=20.0, triton_wall_us=40.0,
+              compile_wall_us=50.0, eager_wall_us=60.0, ours_graph_us=2.0, triton_graph_us=1.9,
+              compile_graph_us=3.0, eager_graph_us=20.0),
+        _cell("rope", batch=32, seq=4096, heads=8, tensor="k", head_dim=128, ulps=0.0),
+        _cell("swiglu", rows=2048, hidden=14336, packed=True, parity=False),
+    ]
+    md = report({"peak_gbs": 6542.7, "reference_package": True, "launches": 20, "blocks": 7, "cells": cells})
+    assert "with n = 20; median of 7 such blocks" in md
+    assert "1 of 5 cells fail AKO's error budget: swiglu bf16 M2048 F14336 packed." in md
+    assert "rope 0 (bit-exact)" in md and "rmsnorm 2," in md
+    # config 1: Triton faster (9 us vs 10 us) -> 0/1 and x0.90
+    assert "| rmsnorm | 1 | 0/1, x0.90 | 1/1, x2.00 | 1/1, x4.00 |" in md
+    # the decode cell is not counted with the throughput cells
+    assert "| rmsnorm_residual | 1 | 1/1, x1.20 | 1/1, x2.00 | 1/1, x4.00 |" in md
+    for cfg in ("## Config 1", "## Config 2", "## Config 3", "## Config 4", "## Decode cells"):
+        assert cfg in md
+    assert "| fp32 | M2048 H4096 | 10 | 100 | 0.500 | 0.90 | 2.00 | 4.00 | 2 |" in md
+    assert "- vs triton: wall clock, ours faster on 1 of 1 cells (x2.00); in a graph, ours at or below on 0 of 1" in md
+
+
+def test_cell_labels() -> None:
+    assert cell_label(_cell("rmsnorm_residual", rows=32, hidden=8192)) == "M32 H8192"
+    assert cell_label(_cell("rope", batch=8, seq=1, heads=32, tensor="q")) == "B8 S1 q(32h)"
+    assert cell_label(_cell("swiglu", rows=64, hidden=5632, packed=False)) == "M64 F5632"
