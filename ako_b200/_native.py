@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int, _c_int]),
     "ako_b200_rope_set_launch": (_c_int, [_c_int]),
     "ako_b200_swiglu_set_launch": (_c_int, [_c_int, _c_int]),
+    "ako_b200_set_pdl": (_c_int, [_c_int]),
     "ako_b200_rmsnorm_set_staging": (_c_int, [_c_int, _c_int, _c_int]),
     "ako_b200_take_device_status": (_c_int, [ctypes.POINTER(ctypes.c_int)]),
 }

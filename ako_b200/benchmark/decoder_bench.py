@@ -1,4 +1,4 @@
-"""Decoder throughput: prefill and decode tokens per second.
+"""Decoder throughput, benchmark configuration 5: prefill and decode tokens per second.
 
 4-layer LLaMA-style stack (d 4096, 32 heads / 8 KV heads, head_dim 128, FFN
 11008, eps 1e-5, theta 1e4, vocab 32000), bf16, random N(0, 0.02) weights.

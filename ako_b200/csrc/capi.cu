@@ -1,4 +1,5 @@
 // Status and error reporting of the C ABI (declared in include/ako_b200.h).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -10,7 +11,10 @@ namespace {
 thread_local char g_last_error[512] = {0};
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices] = {0};
+std::atomic<int> g_pdl{1};
 }  // namespace
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
 int set_error(int status, const char* fmt, ...) {
     va_list ap;
@@ -62,5 +66,7 @@ const char* ako_b200_status_string(int status) {
 }
 
 const char* ako_b200_last_error(void) { return ako_b200::g_last_error; }
+
+int ako_b200_set_pdl(int enable) { return ako_b200::g_pdl.exchange(enable ? 1 : 0); }
 
 }  // extern "C"

@@ -12,6 +12,16 @@
 
 namespace ako_b200 {
 
+// ------------------------------------------------- programmatic dependent launch
+// First statement of every kernel: waits until the previous grid in the
+// stream has completed and its writes are visible (returns at once when the
+// launch was not programmatic), then lets the next kernel's CTAs be scheduled
+// (they wait the same way before touching memory).
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- conversions
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }

@@ -21,6 +21,47 @@ int check_launch(const char* kernel);
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Whether launches carry programmatic stream serialization (see launch_ex).
+bool pdl_enabled();
+
+// Launches kernel(a) on `grid` x `block` with `smem` bytes of dynamic shared
+// memory, in clusters of `cluster` CTAs along x when cluster > 1. With
+// programmatic dependent launch enabled, the kernel may begin while the
+// previous kernel in the stream drains; every kernel of this library waits
+// for that grid (griddepcontrol.wait) before its first global memory access,
+// so results are unchanged and only the launch gap is hidden.
+template <typename Args>
+int launch_ex(void (*kernel)(Args), dim3 grid, dim3 block, size_t smem, int cluster, cudaStream_t st, const Args& a,
+              const char* name) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (cluster > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = n ? attr : nullptr;
+    cfg.numAttrs = n;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(AKO_B200_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(err));
+    }
+    return check_launch(name);
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // True when a row stride of `stride` elements of `elem` bytes keeps every row

@@ -87,6 +87,7 @@ rms_rows_kernel(const RmsArgs a) {
     using P = Packed<T, VEC>;
     __shared__ float scratch[THREADS / 32 > 0 ? THREADS / 32 : 1];
     __shared__ float cluster_part;
+    pdl_enter();
 
     const int lane = threadIdx.x % TPR;
     const int64_t row = CLUSTER > 1 ? static_cast<int64_t>(blockIdx.x / CLUSTER)
@@ -229,6 +230,7 @@ constexpr int kGenericThreads = 256;
 template <typename T, bool RES>
 __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsArgs a) {
     __shared__ float scratch[kGenericThreads / 32];
+    pdl_enter();
     const int64_t row = blockIdx.x;
     const T* xr = static_cast<const T*>(a.x) + row * a.sx;
     const T* rr = RES ? static_cast<const T*>(a.r) + row * a.sr : nullptr;
@@ -263,26 +265,7 @@ template <typename Kernel>
 int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, const RmsArgs& a, cudaStream_t st,
                        const char* name) {
     if (grid > 0x7fffffff) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: too many rows", name);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    if (cluster > 1) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = cluster;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-    }
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return set_error(AKO_B200_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(err));
-    }
-    return check_launch(name);
+    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), 0, cluster, st, a, name);
 }
 
 #define AKO_RMS_CASE(T, RES, CL, TPR, NV)                                                     \
@@ -370,8 +353,8 @@ int launch_rms_rows(const RmsArgs& a, int cluster, int tpr, int nv, cudaStream_t
 
 template <typename T, bool RES>
 int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
-    rms_generic_kernel<T, RES><<<static_cast<unsigned>(a.rows), kGenericThreads, 0, st>>>(a);
-    return check_launch(RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)");
+    return launch_ex(rms_generic_kernel<T, RES>, dim3(static_cast<unsigned>(a.rows)), dim3(kGenericThreads), 0, 1, st,
+                     a, RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)");
 }
 
 // Persistent variant with rows staged in shared memory by bulk copies

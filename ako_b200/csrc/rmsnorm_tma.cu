@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ uint64_t full[kMaxStages];
     __shared__ float scratch[2][WARPS];
+    pdl_enter();
     const RmsArgs& a = t.a;
     const int h = a.h;
     const uint32_t row_bytes = static_cast<uint32_t>(h) * sizeof(T);
@@ -185,8 +186,8 @@ int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
     }
     int64_t grid = static_cast<int64_t>(sm_count()) * ctas_per_sm;
     if (grid > a.rows) grid = a.rows;
-    kernel<<<static_cast<unsigned>(grid), kTmaThreads, smem, st>>>(t);
-    return check_launch(RES ? "rmsnorm_residual(staged)" : "rmsnorm(staged)");
+    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), dim3(kTmaThreads), smem, 1, st, t,
+                     RES ? "rmsnorm_residual(staged)" : "rmsnorm(staged)");
 }
 
 template <typename T, bool RES>

@@ -89,6 +89,7 @@ template <typename T, int NP, bool INTERLEAVED, int HPT>
 __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
     constexpr int E = INTERLEAVED ? 2 * NP : NP;  // elements per 16-byte access
     using P = Packed<T, E>;
+    pdl_enter();
     const int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.z + threadIdx.z;
     if (pos >= a.n_pos) return;
     const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
 // Any alignment and head_dim: one pair per thread, element accesses.
 template <typename T, bool INTERLEAVED>
 __global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeArgs a) {
+    pdl_enter();
     const int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.z + threadIdx.z;
     if (pos >= a.n_pos) return;
     const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
@@ -182,12 +184,10 @@ dim3 rope_block(int chunks, int head_groups, int64_t n_pos) {
     return dim3(bx, by, bz);
 }
 
-template <typename Kernel>
-int launch_rope(Kernel kernel, const RopeArgs& a, dim3 block, cudaStream_t st, const char* name) {
+int launch_rope(void (*kernel)(RopeArgs), const RopeArgs& a, dim3 block, cudaStream_t st, const char* name) {
     const int64_t grid = (a.n_pos + block.z - 1) / block.z;
     if (grid > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: too many positions", name);
-    kernel<<<static_cast<unsigned>(grid), block, 0, st>>>(a);
-    return check_launch(name);
+    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), block, 0, 1, st, a, name);
 }
 
 template <typename T, int NP, bool IL>

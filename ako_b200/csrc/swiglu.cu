@@ -65,6 +65,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // (NARROW, total < 2^32) or a 64-bit division.
 template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW, int THREADS>
 __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
+    pdl_enter();
     using P = Packed<T, VEC>;
     const T* gp = static_cast<const T*>(a.g);
     const T* up = static_cast<const T*>(a.u);
@@ -132,16 +133,13 @@ int launch(SwigluArgs a, bool flat, cudaStream_t st) {
     int64_t grid = (a.total + per_cta - 1) / per_cta;
     const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / THREADS);  // a full SM's worth of threads each
     if (grid > cap) grid = cap;
-    const unsigned g = static_cast<unsigned>(grid);
-    if (flat) {
-        swiglu_kernel<T, VEC, UNROLL, true, true, THREADS><<<g, THREADS, 0, st>>>(a);
-    } else if (a.total <= static_cast<int64_t>(UINT_MAX)) {
+    const dim3 g(static_cast<unsigned>(grid));
+    if (flat) return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
+    if (a.total <= static_cast<int64_t>(UINT_MAX)) {
         a.row_div = FastDiv::make(static_cast<uint32_t>(a.per_row));
-        swiglu_kernel<T, VEC, UNROLL, false, true, THREADS><<<g, THREADS, 0, st>>>(a);
-    } else {
-        swiglu_kernel<T, VEC, UNROLL, false, false, THREADS><<<g, THREADS, 0, st>>>(a);
+        return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, true, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
     }
-    return check_launch("swiglu");
+    return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
 }
 
 template <typename T, int VEC>

@@ -1,6 +1,6 @@
 """LLaMA-style decoder with RMSNorm, RoPE and SwiGLU on the sm_100a kernels.
 
-The caller of the hot path that BASELINE config 5 measures (reference:
+The caller of the hot path that benchmark configuration 5 measures (reference:
 ``ako/models/decoder.py:37-335``): a stack of pre-norm blocks —
 ``norm -> attention -> norm -> SwiGLU MLP`` with the residual carried through
 the fused residual-add RMSNorm — plus the token embedding and LM head the

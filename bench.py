@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 kernels behind AKO's dispatcher API; prints ONE JSON line.
 
-Metric (BASELINE.json): achieved HBM GB/s = algorithmic bytes / device time.
+Metric: achieved HBM GB/s = algorithmic bytes / device time.
 A step is one pass of the hot path over one batch: by default one fused
 residual-add RMSNorm (``rmsnorm_residual``) over config 2's largest cell,
 32768 rows x 16384 bf16 per GPU (4.3 GB moved per step, far above the 126 MB
@@ -19,7 +19,7 @@ L2, so back-to-back steps need no flush).
   ncu summary of this workload.
 * ``cpu_baseline``: the C oracle (a restatement of AKO's unfused reference,
   all host threads) on a bounded row sample of the same workload, rank 0, N=1.
-* ``ops``: the other ops at their largest BASELINE cell (N=1), device time
+* ``ops``: the other ops at their largest benchmark cell (N=1), device time
   per call from a cold L2 (differential timing).
 
 Multi-GPU (torchrun): every rank owns its own row shard (weak scaling); no

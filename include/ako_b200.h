@@ -209,6 +209,17 @@ int ako_b200_rope_set_launch(int heads_per_thread);
  */
 int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
 
+/*
+ * Programmatic dependent launch: with `enable` = 1 (the default) every
+ * kernel of this library is launched with programmatic stream serialization,
+ * so it may start while the previous kernel in the stream drains; it waits
+ * for that kernel's completion before touching memory, so results do not
+ * change. 0 launches with plain stream order. Returns the previous setting.
+ * Not part of the reference's interface; it has no counterpart there.
+ * Process-wide.
+ */
+int ako_b200_set_pdl(int enable);
+
 #ifdef __cplusplus
 }
 #endif

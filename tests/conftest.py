@@ -38,7 +38,9 @@ def cuda_device():
 
 
 def reference_path() -> Path | None:
-    """Source tree of the reference, when this machine has one (never on GPU boxes)."""
+    """Source tree of the reference (``AKO_REFERENCE``, else the build
+    container's read-only copy), when this machine has one; GPU boxes have
+    none, and only CPU tests use it."""
     cand = os.environ.get("AKO_REFERENCE", "/root/reference")
     p = Path(cand)
     return p if (p / "ako" / "__init__.py").exists() else None

@@ -129,6 +129,12 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path) -> None:
         _native.lib()
 
 
+def test_pdl_switch_returns_previous_setting(lib) -> None:
+    assert lib.ako_b200_set_pdl(0) == 1  # on by default
+    assert lib.ako_b200_set_pdl(5) == 0
+    assert lib.ako_b200_set_pdl(1) == 1
+
+
 def test_rope_launch_override_validation(lib) -> None:
     assert lib.ako_b200_rope_set_launch(2) == 0
     assert lib.ako_b200_rope_set_launch(0) == 0

@@ -360,6 +360,45 @@ def test_swiglu_extremes(cuda_device) -> None:
 
 
 # ------------------------------------------------------- launch semantics
+def test_programmatic_launch_changes_no_result(cuda_device) -> None:
+    """Every kernel runs with and without programmatic dependent launch; chains
+    of dependent calls (each reads the previous call's output) give identical
+    bytes both ways, eagerly and in a CUDA graph."""
+    lib = _native.lib()
+    cos, sin = (to_torch(t, O.F32, cuda_device) for t in O.build_rope_tables(96, 128))
+    x = torch.randn(96, 4096, device=cuda_device, dtype=torch.bfloat16)
+    r = torch.randn_like(x)
+    w = torch.randn(4096, device=cuda_device, dtype=torch.bfloat16)
+
+    def chain():
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+        y2 = kernels.rmsnorm_cuda_sm100(ro, w, 1e-6)
+        q = kernels.rope_cuda_sm100(y2.view(1, 96, 32, 128), cos[:96], sin[:96], "neox")
+        return kernels.swiglu_cuda_sm100(q.view(96, 4096), y)
+
+    try:
+        outs = {}
+        for pdl in (0, 1):
+            lib.ako_b200_set_pdl(pdl)
+            eager = chain()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                chain()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                captured = chain()
+            graph.replay()
+            torch.cuda.synchronize()
+            outs[pdl] = (eager.clone(), captured.clone())
+            del graph
+        assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][0], outs[0][1])
+        assert torch.equal(outs[1][0], outs[1][1])
+    finally:
+        lib.ako_b200_set_pdl(1)
+
+
 def test_runs_on_the_current_stream_and_in_a_graph(cuda_device) -> None:
     x = torch.randn(64, 4096, device=cuda_device, dtype=torch.bfloat16)
     r = torch.randn_like(x)
@@ -389,7 +428,7 @@ def test_wrong_device_and_dtype_errors(cuda_device) -> None:
         kernels.rmsnorm_cuda_sm100(x.float(), torch.ones(64))
 
 
-# ------------------------------------------------- full BASELINE sizes
+# ------------------------------------------------- full benchmark sizes
 def test_full_size_residual_against_torch_fp32(cuda_device) -> None:
     """Config 2's largest cell (32768 x 16384 bf16): the rounded residual is
     exact against torch's own add; the norm is within budget of an fp32 torch
