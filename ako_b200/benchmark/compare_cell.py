@@ -6,7 +6,12 @@ side-by-side profiling (``ncu -k regex:...``) of the two kernels.
 The competitor is the reference's Triton kernel when the reference package
 is importable (``--reference-path``), else ``torch.compile`` of the unfused
 reference. Each is launched ``--launches`` times after three warm-up calls,
-with a 2 x L2 read between launches so every launch starts with a cold L2.
+with a 2 x L2 read between launches so every launch starts with a cold L2;
+the measured launches sit in an NVTX range named ``measured``:
+
+    ncu --set full --clock-control none --nvtx --nvtx-include "measured/" \
+        -k regex:"rms_rows_kernel|_rmsnorm_kernel_impl" -c 2 -o prof \
+        python -m ako_b200.benchmark.compare_cell --op rmsnorm --rows 2048 --hidden 4096 --dtype fp32 --launches 1
 """
 
 from __future__ import annotations
@@ -55,12 +60,16 @@ def main() -> None:
             "swiglu": lambda: kernels.swiglu_cuda_sm100(x, r)}[args.op]
     flush = torch.empty(2 * 126 * 2**20, dtype=torch.uint8, device=dev)
     sink = torch.empty((), dtype=torch.int64, device=dev)
-    for fn in (ours, comp):
+    for fn in (ours, comp):  # warm-up (and the competitor's autotuning) first
         for _ in range(3):
             fn()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("measured")  # ncu --nvtx --nvtx-include "measured/" selects these launches
+    for fn in (ours, comp):
         for _ in range(args.launches):
             torch.sum(flush.view(torch.int64), dim=0, out=sink)
             fn()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     print("ok")
 
