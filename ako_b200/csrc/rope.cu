@@ -10,8 +10,9 @@
 // and only the final cast rounds.
 //
 // Work decomposition: a CTA slice per sequence position (b, s). A thread owns
-// a chunk of NP consecutive pairs of the head vector; it loads the NP cos/sin
-// values of that chunk once and applies them to every head it visits — the
+// NP pairs of the head vector (neox: NP consecutive pairs; interleaved: two
+// 16-byte chunks of NP/2 pairs, a head's thread count apart); it loads their
+// NP cos/sin values once and applies them to every head it visits — the
 // heads of up to two tensors (q then k for rope_qk), so a q/k pair shares one
 // table read and one launch. Threads in a warp cover consecutive chunks of
 // consecutive heads, so every 16-byte access of a warp falls in full
@@ -47,7 +48,7 @@ struct RopeArgs {
 int g_heads_per_thread = 0;  // 0: built-in choice
 
 template <int N>
-__device__ __forceinline__ void load_table(const float* p, float (&out)[N]) {
+__device__ __forceinline__ void load_table(const float* p, float* out) {
     if constexpr (N % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < N; k += 4) {
@@ -82,22 +83,33 @@ __device__ __forceinline__ void head_rows(const RopeArgs& a, int h, int64_t b, i
 }
 
 // Vector path: thread (x = chunk, y = head group, z = position in the CTA)
-// owns NP consecutive pairs of HPT consecutive heads. Its NP cos/sin values
-// are loaded once; the 16-byte loads of all its heads are issued before any
-// arithmetic.
+// owns NP pairs of HPT consecutive heads. Its NP cos/sin values are loaded
+// once; the 16-byte loads of all its heads are issued before any arithmetic.
 template <typename T, int NP, bool INTERLEAVED, int HPT>
 __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
-    constexpr int E = INTERLEAVED ? 2 * NP : NP;  // elements per 16-byte access
+    constexpr int E = NP;  // elements per 16-byte access
     using P = Packed<T, E>;
     pdl_enter();
     const int64_t pos = static_cast<int64_t>(blockIdx.x) * blockDim.z + threadIdx.z;
     if (pos >= a.n_pos) return;
     const uint32_t b = a.seq.div(static_cast<uint32_t>(pos));
     const int64_t s = static_cast<int64_t>(static_cast<uint32_t>(pos) - b * a.seq.d);
-    const int p0 = threadIdx.x * NP;  // blockDim.x == chunks per head
+    // neox: pairs [p0, p0 + NP) of both halves. interleaved: the 16-byte
+    // chunks threadIdx.x and threadIdx.x + blockDim.x of the row (NP/2 pairs
+    // each), so each warp access covers whole 128-byte lines.
+    const int p0 = threadIdx.x * NP;  // blockDim.x == threads per head
+    constexpr int Q = NP / 2;         // pairs per interleaved chunk
+    const int c0 = threadIdx.x * E, c1 = (threadIdx.x + blockDim.x) * E;  // interleaved element offsets
     float cs[NP], sn[NP];
-    load_table<NP>(a.cos + s * a.ts + p0, cs);
-    load_table<NP>(a.sin + s * a.ts + p0, sn);
+    if constexpr (INTERLEAVED) {
+        load_table<Q>(a.cos + s * a.ts + c0 / 2, cs);
+        load_table<Q>(a.cos + s * a.ts + c1 / 2, cs + Q);
+        load_table<Q>(a.sin + s * a.ts + c0 / 2, sn);
+        load_table<Q>(a.sin + s * a.ts + c1 / 2, sn + Q);
+    } else {
+        load_table<NP>(a.cos + s * a.ts + p0, cs);
+        load_table<NP>(a.sin + s * a.ts + p0, sn);
+    }
     const int heads = a.t0.heads + a.t1.heads;
 
     for (int h0 = threadIdx.y * HPT; h0 < heads; h0 += blockDim.y * HPT) {
@@ -109,7 +121,8 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
                 const T* xp;
                 head_rows<T>(a, h0 + j, b, s, xp, yrow[j]);
                 if constexpr (INTERLEAVED) {
-                    lo[j] = ld_stream_no_l1<T, E>(xp + 2 * p0);
+                    lo[j] = ld_stream_no_l1<T, E>(xp + c0);
+                    hi[j] = ld_stream_no_l1<T, E>(xp + c1);
                 } else {
                     lo[j] = ld_stream_no_l1<T, E>(xp + p0);
                     hi[j] = ld_stream_no_l1<T, E>(xp + a.half + p0);
@@ -121,13 +134,17 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
             if (h0 + j < heads) {
                 T* yp = yrow[j];
                 if constexpr (INTERLEAVED) {
-                    P o;
+                    P ol, oh;
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) {
+                    for (int k = 0; k < Q; ++k) {
                         const float2 v = get2<T, E>(lo[j], 2 * k);
-                        put2<T, E>(o, 2 * k, rot_lo(v.x, v.y, cs[k], sn[k]), rot_hi(v.x, v.y, cs[k], sn[k]));
+                        const float2 w = get2<T, E>(hi[j], 2 * k);
+                        put2<T, E>(ol, 2 * k, rot_lo(v.x, v.y, cs[k], sn[k]), rot_hi(v.x, v.y, cs[k], sn[k]));
+                        put2<T, E>(oh, 2 * k, rot_lo(w.x, w.y, cs[Q + k], sn[Q + k]),
+                                   rot_hi(w.x, w.y, cs[Q + k], sn[Q + k]));
                     }
-                    st_global<T, E>(yp + 2 * p0, o);
+                    st_global<T, E>(yp + c0, ol);
+                    st_global<T, E>(yp + c1, oh);
                 } else {
                     P ol, oh;
 #pragma unroll
@@ -205,16 +222,15 @@ template <typename T>
 int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st, const char* name) {
     constexpr int VEC = 16 / sizeof(T);
     const int heads = a.t0.heads + a.t1.heads;
-    // Heads per thread: two heads share a thread's table values and keep more
-    // loads in flight, which is fastest once the grid fills the GPU (8..40
-    // heads at D = 128); a grid smaller than one wave of threads (decode:
-    // a few positions) finishes sooner with one head per thread.
-    const int64_t threads_one_head = a.n_pos * heads * (a.half / (interleaved ? VEC / 2 : VEC));
-    const bool small = threads_one_head < static_cast<int64_t>(sm_count()) * 2048;
-    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : ((heads >= 8 && !small) ? 2 : 1);
-    const int chunk_pairs = interleaved ? VEC / 2 : VEC;
-    if (vector_ok && a.half % chunk_pairs == 0 && a.half / chunk_pairs <= 256) {
-        if (interleaved) return launch_vec<T, VEC / 2, true>(a, hpt, st, name);
+    // Heads per thread, measured on B200 (D = 128, 8..40 heads, 1 to 131072
+    // positions): neox is fastest with one (3-4.5% over two at full size,
+    // more for decode grids); interleaved with two (17-20% over one), whose
+    // four 16-byte accesses per thread then sit a warp width apart.
+    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (interleaved ? 2 : 1);
+    // A thread rotates VEC pairs of a head: two 16-byte accesses, one in each
+    // half (neox) or two chunks that are a head's threads apart (interleaved).
+    if (vector_ok && a.half % VEC == 0 && a.half / VEC <= 256) {
+        if (interleaved) return launch_vec<T, VEC, true>(a, hpt, st, name);
         return launch_vec<T, VEC, false>(a, hpt, st, name);
     }
     const dim3 block = rope_block(a.half < 256 ? a.half : 256, heads, a.n_pos);
