@@ -167,19 +167,24 @@ def max_over_ranks(v: float, world: int, device: torch.device) -> float:
     return sharding.max_over_ranks(v, device)
 
 
-def timed_region(step, k: int, w: int, world: int) -> float:
-    """W untimed steps, then exactly K steps between events; ms on this rank."""
+def timed_region(step, k: int, w: int, world: int, marks=None) -> float:
+    """W untimed steps, then exactly K steps between events; ms on this rank.
+    ``marks`` (a clock sampler) gets the host times around the timed steps."""
     for _ in range(w):
         step()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if marks is not None:
+        marks.mark_start()
     start.record()
     for _ in range(k):
         step()
     end.record()
     torch.cuda.synchronize()
+    if marks is not None:
+        marks.mark_end()
     barrier(world)
     return start.elapsed_time(end)
 
@@ -315,11 +320,11 @@ def main() -> None:
     device = torch.device("cuda", local)
     peak, peak_src = hbm_peak()
 
-    from ako_b200.benchmark.clocks import ClockSampler
+    from ako_b200.benchmark.clocks import start_sampler
 
     wl = Workload(args.workload, device, seed=rank)
-    sampler = ClockSampler(local).start()
-    ms = timed_region(wl.step, args.steps, args.warmup, world)
+    sampler = start_sampler(local)
+    ms = timed_region(wl.step, args.steps, args.warmup, world, marks=sampler)
     clocks = sampler.stop()
     ms_max = max_over_ranks(ms, world, device)
     per_step_ms = ms_max / args.steps

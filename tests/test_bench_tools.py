@@ -77,3 +77,22 @@ def test_cell_labels() -> None:
     assert cell_label(_cell("rmsnorm_residual", rows=32, hidden=8192)) == "M32 H8192"
     assert cell_label(_cell("rope", batch=8, seq=1, heads=32, tensor="q")) == "B8 S1 q(32h)"
     assert cell_label(_cell("swiglu", rows=64, hidden=5632, packed=False)) == "M64 F5632"
+
+
+def test_clock_summary_window_and_reasons() -> None:
+    from ako_b200.benchmark.clocks import summarize
+
+    # (time, sm MHz, max MHz, watts, utilization %, reason mask)
+    samples = [(0.0, 1965.0, 1965.0, 300.0, 100.0, 0x4), (0.5, 1900.0, 1965.0, 310.0, 100.0, 0),
+               (0.6, 1920.0, 1965.0, 305.0, 100.0, 0x40), (1.5, 800.0, 1965.0, 50.0, 0.0, 0x1)]
+    inside = summarize(samples, (0.4, 0.7), "test")
+    assert inside["samples"] == 2 and inside["samples_in_timed_region"] == 2
+    assert inside["sm_mhz"] == 1910.0 and inside["reasons"] == ["hw_thermal_slowdown"]
+    assert inside["rejecting_reason_seen"] is True
+    whole = summarize(samples, None, "test")
+    assert whole["samples_under_load"] == 3 and whole["sm_max_mhz"] == 1965.0
+    assert whole["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]  # gpu_idle is never reported
+    # an empty window falls back to every sample and says so
+    empty = summarize(samples, (5.0, 6.0), "test")
+    assert empty["samples_in_timed_region"] == 0 and empty["samples"] == 4
+    assert summarize([], None)["samples"] == 0
