@@ -144,13 +144,17 @@ int launch(SwigluArgs a, bool flat, cudaStream_t st) {
 
 template <typename T, int VEC>
 int launch_vec(const SwigluArgs& a, bool flat, cudaStream_t st) {
-    // Large problems keep two vectors per thread in flight in 256-thread CTAs;
-    // small ones (decode rows) use one vector per thread in 128-thread CTAs,
-    // so the few vectors spread over many SMs (measured fastest up to ~64
-    // rows of 5632..14336).
+    // 256-thread CTAs with one vector of each input per thread (32 registers,
+    // a full SM of threads) are within 1% of the best shape on every cell
+    // measured on B200 (F 5632..14336, 2048..16384 rows, bf16 and fp16) and
+    // up to 10% faster than two vectors per thread, except dense operands of
+    // 2^24 vectors and more, which stream 2-4% faster with two. Small problems
+    // (decode rows) use 128-thread CTAs, so the few vectors spread over many
+    // SMs (measured fastest up to ~64 rows of 5632..14336).
     const bool small = a.total < static_cast<int64_t>(sm_count()) * kThreads * 4;
+    const bool huge_dense = flat && a.total >= (int64_t{1} << 24);
     const int threads = g_threads > 0 ? g_threads : (small ? 128 : kThreads);
-    const int unroll = g_unroll > 0 ? g_unroll : (small ? 1 : 2);
+    const int unroll = g_unroll > 0 ? g_unroll : (huge_dense ? 2 : 1);
     switch (threads * 16 + unroll) {
         case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, st);
         case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, st);
