@@ -232,8 +232,9 @@ def test_rope_shapes(cuda_device, dtype: str, style: str, shape) -> None:
     np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
 
 
+@pytest.mark.parametrize("style", O.ROPE_STYLES)
 @pytest.mark.parametrize("dtype", (O.F16, O.BF16))
-def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str) -> None:
+def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str, style: str) -> None:
     """q stored (B, H, S, D) and passed as .transpose(1, 2); decode-style
     table slice cos[2047:2048] of an 8192-row table; neither is copied."""
     rng = np.random.default_rng(21)
@@ -242,10 +243,10 @@ def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str) -> N
     for b, hh, s, off in ((4, 32, 1, 2047), (2, 8, 33, 100)):
         q_bhsd = normal(rng, (b, hh, s, 128), 0, 1, dtype)
         q = to_torch(q_bhsd, dtype, cuda_device).transpose(1, 2)
-        y = kernels.rope_cuda_sm100(q, cos_d[off:off + s], sin_d[off:off + s], "neox")
+        y = kernels.rope_cuda_sm100(q, cos_d[off:off + s], sin_d[off:off + s], style)
         assert y.stride() == q.stride()  # the output keeps the (B, H, S, D) layout
         ref = O.rope(np.ascontiguousarray(q_bhsd.transpose(0, 2, 1, 3)), cos_full[off:off + s],
-                     sin_full[off:off + s], "neox", dtype)
+                     sin_full[off:off + s], style, dtype)
         np.testing.assert_array_equal(to_numpy(y), ref)
 
 
