@@ -219,7 +219,7 @@ int launch_vec(const RopeArgs& a, int hpt, cudaStream_t st, const char* name) {
 }
 
 template <typename T>
-int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st, const char* name) {
+int run(const RopeArgs& a, bool interleaved, int access_bytes, cudaStream_t st, const char* name) {
     constexpr int VEC = 16 / sizeof(T);
     const int heads = a.t0.heads + a.t1.heads;
     // Heads per thread, measured on B200 (D = 128, 8..40 heads, 1 to 131072
@@ -227,11 +227,21 @@ int run(const RopeArgs& a, bool interleaved, bool vector_ok, cudaStream_t st, co
     // more for decode grids); interleaved with two (17-20% over one), whose
     // four 16-byte accesses per thread then sit a warp width apart.
     const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (interleaved ? 2 : 1);
-    // A thread rotates VEC pairs of a head: two 16-byte accesses, one in each
-    // half (neox) or two chunks that are a head's threads apart (interleaved).
-    if (vector_ok && a.half % VEC == 0 && a.half / VEC <= 256) {
-        if (interleaved) return launch_vec<T, VEC, true>(a, hpt, st, name);
-        return launch_vec<T, VEC, false>(a, hpt, st, name);
+    // A thread rotates NP pairs of a head with two accesses of access_bytes:
+    // one in each half (neox) or two chunks a head's thread count apart
+    // (interleaved). 16-byte accesses where every operand allows them, else
+    // 8 or 4 bytes (at least two elements).
+    const int np = access_bytes / static_cast<int>(sizeof(T));
+    if (np == VEC) return interleaved ? launch_vec<T, VEC, true>(a, hpt, st, name) : launch_vec<T, VEC, false>(a, hpt, st, name);
+    if constexpr (VEC / 2 >= 2) {
+        if (np == VEC / 2)
+            return interleaved ? launch_vec<T, VEC / 2, true>(a, hpt, st, name)
+                               : launch_vec<T, VEC / 2, false>(a, hpt, st, name);
+    }
+    if constexpr (VEC / 4 >= 2) {
+        if (np == VEC / 4)
+            return interleaved ? launch_vec<T, VEC / 4, true>(a, hpt, st, name)
+                               : launch_vec<T, VEC / 4, false>(a, hpt, st, name);
     }
     const dim3 block = rope_block(a.half < 256 ? a.half : 256, heads, a.n_pos);
     if (interleaved) return launch_rope(rope_scalar_kernel<T, true>, a, block, st, name);
@@ -278,11 +288,32 @@ bool make_tensor(RopeTensor& t, const void* x, int64_t xb, int64_t xs, int64_t x
     return true;
 }
 
-bool vector_ok(const RopeTensor& t, int es) {
+bool aligned_to(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
+
+// Every access of tensor `t` at `bytes` width starts on a multiple of it.
+bool tensor_ok(const RopeTensor& t, int es, int bytes) {
     if (t.heads == 0) return true;
-    auto s16 = [es](int64_t st) { return ((st * es) & 15) == 0; };
-    return aligned16(t.x) && aligned16(t.y) && s16(t.xb) && s16(t.xs) && s16(t.xh) && s16(t.yb) && s16(t.ys) &&
-           s16(t.yh);
+    auto ok = [es, bytes](int64_t st) { return ((st * es) & (bytes - 1)) == 0; };
+    return aligned_to(t.x, bytes) && aligned_to(t.y, bytes) && ok(t.xb) && ok(t.xs) && ok(t.xh) && ok(t.yb) &&
+           ok(t.ys) && ok(t.yh);
+}
+
+// Widest access (16, 8 or 4 bytes, at least two elements) that the tensors,
+// the half head size and the table rows all allow; 0 for the scalar kernel.
+// A thread reads its table values as float4 (4+ per group), float2 (2) or
+// floats (1), where a group is its NP pairs (neox) or NP/2 (interleaved).
+int access_bytes(const RopeArgs& a, int64_t half, int es, bool interleaved) {
+    for (int bytes = 16; bytes >= 4; bytes /= 2) {
+        const int np = bytes / es;
+        if (np < 2) break;
+        if (half % np != 0 || half / np > 256) continue;
+        const int group = interleaved ? np / 2 : np;
+        const int tb = group >= 4 ? 16 : (group == 2 ? 8 : 4);
+        if (tensor_ok(a.t0, es, bytes) && tensor_ok(a.t1, es, bytes) && aligned_to(a.cos, tb) &&
+            aligned_to(a.sin, tb) && ((a.ts * 4) & (tb - 1)) == 0)
+            return bytes;
+    }
+    return 0;
 }
 
 int dispatch(RopeArgs& a, const RopeCall& c, void* stream, const char* name) {
@@ -290,14 +321,13 @@ int dispatch(RopeArgs& a, const RopeCall& c, void* stream, const char* name) {
     a.half = static_cast<int>(c.half);
     a.n_pos = c.batch * c.seq;
     a.seq = FastDiv::make(static_cast<uint32_t>(c.seq));
-    const bool vec = vector_ok(a.t0, es) && vector_ok(a.t1, es) && aligned16(a.cos) && aligned16(a.sin) &&
-                     ((a.ts * 4) & 15) == 0 && (c.half * es) % 16 == 0;
     const bool il = c.style == AKO_B200_ROPE_INTERLEAVED;
+    const int bytes = access_bytes(a, c.half, es, il);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (c.dtype) {
-        case AKO_B200_F32: return run<float>(a, il, vec, st, name);
-        case AKO_B200_F16: return run<__half>(a, il, vec, st, name);
-        default: return run<__nv_bfloat16>(a, il, vec, st, name);
+        case AKO_B200_F32: return run<float>(a, il, bytes, st, name);
+        case AKO_B200_F16: return run<__half>(a, il, bytes, st, name);
+        default: return run<__nv_bfloat16>(a, il, bytes, st, name);
     }
 }
 

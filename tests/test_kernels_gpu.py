@@ -216,7 +216,9 @@ def test_rmsnorm_rejects_oversized_hidden_dim(cuda_device) -> None:
 
 # -------------------------------------------------------------------- rope
 ROPE_SHAPES = [(2, 6, 3, 8), (1, 1, 32, 128), (8, 1, 8, 128), (2, 128, 8, 64), (1, 64, 32, 128),
-               (3, 17, 5, 128), (2, 9, 4, 256), (1, 5, 2, 6), (2, 4, 3, 2)]
+               (3, 17, 5, 128), (2, 9, 4, 256), (1, 5, 2, 6), (2, 4, 3, 2),
+               # half head sizes that take 8-byte (36 pairs) and 4-byte (50, 10 pairs) accesses
+               (2, 9, 3, 100), (1, 7, 4, 72), (2, 5, 6, 20)]
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -230,6 +232,21 @@ def test_rope_shapes(cuda_device, dtype: str, style: str, shape) -> None:
     y = kernels.rope_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(cos, O.F32, cuda_device),
                                 to_torch(sin, O.F32, cuda_device), style)
     np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
+
+
+@pytest.mark.parametrize("style", O.ROPE_STYLES)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rope_views_at_every_alignment(cuda_device, dtype: str, style: str) -> None:
+    """Views starting 0..3 elements into a padded buffer: each start selects a
+    different access width (16, 8, 4 bytes or element accesses)."""
+    rng = np.random.default_rng(31)
+    b, s, hh, d = 2, 9, 5, 128
+    cos, sin = O.build_rope_tables(s, d, offset=7)
+    base = to_torch(normal(rng, (b, s, hh, d + 8), 0, 1, dtype), dtype, cuda_device)
+    for off in range(4):
+        x = base[..., off:off + d]
+        y = kernels.rope_cuda_sm100(x, to_torch(cos, O.F32, cuda_device), to_torch(sin, O.F32, cuda_device), style)
+        np.testing.assert_array_equal(to_numpy(y), O.rope(to_numpy(x), cos, sin, style, dtype), err_msg=f"offset {off}")
 
 
 @pytest.mark.parametrize("style", O.ROPE_STYLES)
