@@ -14,9 +14,10 @@
 //    the row is read from HBM once and written once. TPR == 32 puts one row
 //    on each warp (4 rows per 128-thread CTA, shuffle-only reduction); larger
 //    TPR puts one row on a CTA (shuffle + one shared-memory exchange).
-//  * rms_generic_kernel: any width and alignment. One CTA per row, scalar
-//    accesses, two passes; the second pass re-reads the row (an L2 hit for
-//    rows up to the L2 size).
+//  * rms_generic_kernel: any width and alignment. One CTA per row, two
+//    passes (the second re-reads the row, an L2 hit for rows up to the L2
+//    size); 16-byte accesses for the part of each row where every operand is
+//    16-byte aligned, element accesses for the rest.
 #pragma once
 
 #include "common.cuh"
@@ -229,17 +230,32 @@ constexpr int kGenericThreads = 256;
 
 template <typename T, bool RES>
 __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsArgs a) {
+    constexpr int VEC = 16 / sizeof(T);
+    using P = Packed<T, VEC>;
     __shared__ float scratch[kGenericThreads / 32];
     pdl_enter();
     const int64_t row = blockIdx.x;
     const T* xr = static_cast<const T*>(a.x) + row * a.sx;
     const T* rr = RES ? static_cast<const T*>(a.r) + row * a.sr : nullptr;
     T* ro = RES ? static_cast<T*>(a.ro) + row * a.sro : nullptr;
+    T* yr = static_cast<T*>(a.y) + row * a.sy;
+
+    // The row splits into a scalar head, a body of 16-byte vectors and a
+    // scalar tail when all of its row pointers sit at the same offset within
+    // 16 bytes (ragged widths, e.g. 8200-byte rows); otherwise it is all head.
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(xr) & 15u;
+    bool same = mis % sizeof(T) == 0 && (reinterpret_cast<uintptr_t>(yr) & 15u) == mis;
+    if constexpr (RES)
+        same = same && (reinterpret_cast<uintptr_t>(rr) & 15u) == mis && (reinterpret_cast<uintptr_t>(ro) & 15u) == mis;
+    int head = same ? static_cast<int>(((16u - mis) & 15u) / sizeof(T)) : a.h;
+    if (head > a.h) head = a.h;
+    const int nvec = (a.h - head) / VEC;
+    const int tail = head + nvec * VEC;
 
     // Rounded squares accumulated in fp64 per thread (any row length stays
     // within one fp32 rounding of the exact sum), then pairwise across threads.
     double acc = 0.0;
-    for (int col = threadIdx.x; col < a.h; col += kGenericThreads) {
+    auto first_pass = [&](int col) {
         float f = to_f32(xr[col]);
         if constexpr (RES) {
             const T s = from_f32<T>(__fadd_rn(f, to_f32(rr[col])));
@@ -247,15 +263,51 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
             f = to_f32(s);
         }
         acc += static_cast<double>(__fmul_rn(f, f));
+    };
+    for (int col = threadIdx.x; col < head; col += kGenericThreads) first_pass(col);
+    for (int col = tail + threadIdx.x; col < a.h; col += kGenericThreads) first_pass(col);
+    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+        const int col = head + v * VEC;
+        P xv = ld_stream<T, VEC>(xr + col);
+        if constexpr (RES) {
+            const P rv = ld_stream<T, VEC>(rr + col);
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 xa = get2<T, VEC>(xv, e);
+                const float2 ra = get2<T, VEC>(rv, e);
+                put2<T, VEC>(xv, e, __fadd_rn(xa.x, ra.x), __fadd_rn(xa.y, ra.y));
+            }
+            st_global<T, VEC>(ro + col, xv);
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; e += 2) {
+            const float2 f = get2<T, VEC>(xv, e);
+            acc += static_cast<double>(__fmul_rn(f.x, f.x));
+            acc += static_cast<double>(__fmul_rn(f.y, f.y));
+        }
     }
     const float total = block_sum<kGenericThreads>(static_cast<float>(acc), scratch);
     const float inv = rms_inv(total, a);
 
-    T* yr = static_cast<T*>(a.y) + row * a.sy;
-    for (int col = threadIdx.x; col < a.h; col += kGenericThreads) {
-        // The residual pass reads back what this same thread stored above.
+    // The residual pass reads back what this same thread stored above, with
+    // ordinary loads so the compiler keeps them after those stores.
+    auto second_pass = [&](int col) {
         const float f = RES ? to_f32(ro[col]) : to_f32(xr[col]);
         yr[col] = from_f32<T>(__fmul_rn(__fmul_rn(f, inv), load_weight(a.w, a.wdtype, col)));
+    };
+    for (int col = threadIdx.x; col < head; col += kGenericThreads) second_pass(col);
+    for (int col = tail + threadIdx.x; col < a.h; col += kGenericThreads) second_pass(col);
+    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+        const int col = head + v * VEC;
+        const P xv = RES ? ld_cached<T, VEC>(ro + col) : ld_cached<T, VEC>(xr + col);
+        P o;
+#pragma unroll
+        for (int e = 0; e < VEC; e += 2) {
+            const float2 f = get2<T, VEC>(xv, e);
+            put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), load_weight(a.w, a.wdtype, col + e)),
+                         __fmul_rn(__fmul_rn(f.y, inv), load_weight(a.w, a.wdtype, col + e + 1)));
+        }
+        st_global<T, VEC>(yr + col, o);
     }
 }
 
