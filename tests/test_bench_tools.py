@@ -96,3 +96,21 @@ def test_clock_summary_window_and_reasons() -> None:
     empty = summarize(samples, (5.0, 6.0), "test")
     assert empty["samples_in_timed_region"] == 0 and empty["samples"] == 4
     assert summarize([], None)["samples"] == 0
+
+
+def test_sweep_cells_cover_the_benchmark_grid() -> None:
+    from ako_b200.benchmark.sweep import cells
+
+    cs = cells({1, 2, 3, 4})
+    by = {c: [x for x in cs if x["config"] == c] for c in (1, 2, 3, 4)}
+    assert [len(by[c]) for c in (1, 2, 3, 4)] == [1, 40, 36, 48] and len(cs) == 125
+    assert by[1][0]["rows"] == 2048 and by[1][0]["hidden"] == 4096 and by[1][0]["dtype"] == "fp32"
+    assert {(c["rows"], c["hidden"]) for c in by[2]} == {(m, h) for m in (1, 32, 512, 8192, 32768)
+                                                          for h in (2048, 4096, 8192, 16384)}
+    assert all(c["decode"] == (c["rows"] <= 32) for c in by[2])
+    assert {(c["batch"], c["seq"], c["heads"]) for c in by[3]} == {(b, s, h) for b in (1, 8, 32)
+                                                                     for s in (1, 512, 4096) for h in (32, 8)}
+    assert all(c["decode"] == (c["seq"] == 1) and c["head_dim"] == 128 for c in by[3])
+    assert {(c["rows"], c["hidden"], c["packed"]) for c in by[4]} == {
+        (m, f, p) for m in (1, 64, 2048, 16384) for f in (5632, 11008, 14336) for p in (False, True)}
+    assert all(c["decode"] == (c["rows"] <= 64) for c in by[4])
