@@ -417,6 +417,46 @@ def test_programmatic_launch_changes_no_result(cuda_device) -> None:
         lib.ako_b200_set_pdl(1)
 
 
+@pytest.mark.parametrize("dtype", (O.BF16, O.F32))
+def test_host_buffer_pipeline_matches_the_device_call(cuda_device, dtype: str) -> None:
+    """The host-buffer entry point (pinned host tensors streamed through the
+    GPU in chunks on three streams), for several chunk and slot counts with a
+    ragged last chunk: the rounded residual equals the device call's bytes;
+    the norm is within the parity gates (a chunk's row count can select
+    another launch shape, whose reduction order differs) and equals the
+    device call's bytes when one chunk holds every row."""
+    from ako_b200 import host
+
+    rng = np.random.default_rng(41)
+    rows, h = 1000, 4096
+    x, r = normal(rng, (rows, h), 0, 1, dtype), normal(rng, (rows, h), 0, 1, dtype)
+    w = normal(rng, (h,), 1, 0.1, dtype)
+    wd = to_torch(w, dtype, cuda_device)
+    yd, rod = kernels.rmsnorm_residual_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(r, dtype, cuda_device),
+                                                  wd, 1e-5)
+    xh, rh = to_torch(x, dtype, "cpu").pin_memory(), to_torch(r, dtype, "cpu").pin_memory()
+    y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+    for chunk_rows, slots in ((96, 3), (333, 2), (1000, 3), (7, 4)):
+        y, ro = host.rmsnorm_residual_host(xh, rh, wd, 1e-5, chunk_rows=chunk_rows, slots=slots)
+        torch.cuda.current_stream().synchronize()
+        what = f"chunks of {chunk_rows}, {slots} slots"
+        assert torch.equal(ro, rod.cpu()), what
+        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+        assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", what)
+        if chunk_rows >= rows:
+            assert torch.equal(y, yd.cpu()), what
+    # preallocated pinned outputs are filled in place
+    y_out = torch.empty_like(xh).pin_memory()
+    ro_out = torch.empty_like(xh).pin_memory()
+    host.rmsnorm_residual_host(xh, rh, wd, 1e-5, y_out=y_out, residual_out=ro_out, chunk_rows=rows)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(y_out, yd.cpu()) and torch.equal(ro_out, rod.cpu())
+    with pytest.raises(ValueError, match="host tensors"):
+        host.rmsnorm_residual_host(xh.to(cuda_device), rh, wd)
+    with pytest.raises(ValueError, match="weight must live"):
+        host.rmsnorm_residual_host(xh, rh, wd.cpu())
+
+
 def test_runs_on_the_current_stream_and_in_a_graph(cuda_device) -> None:
     x = torch.randn(64, 4096, device=cuda_device, dtype=torch.bfloat16)
     r = torch.randn_like(x)
