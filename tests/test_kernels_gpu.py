@@ -537,3 +537,53 @@ def test_full_size_rope_and_swiglu_properties(cuda_device) -> None:
         ref = (torch.nn.functional.silu(g[lo:lo + 2048].float()) * u[lo:lo + 2048].float()).to(torch.bfloat16)
         diff = (ref.float() - out[lo:lo + 2048].float()).abs().max().item()
         assert diff <= 1e-5 + 1.6e-2 * ref.float().abs().max().item()
+
+
+# ------------------------------------------------------------- randomized
+def _view(base: torch.Tensor, rows: int, width: int, stride: int, off: int) -> torch.Tensor:
+    """rows x width view with row stride `stride`, starting `off` elements into the flat `base`."""
+    return base[off:].as_strided((rows, width), (stride, 1))
+
+
+def test_randomized_shapes_and_offsets_against_oracle(cuda_device) -> None:
+    """Seeded random widths, row counts, dtypes, row paddings and view offsets
+    (every access width and the scalar paths), all three ops against the
+    oracle."""
+    rng = np.random.default_rng(2026)
+    for case in range(48):
+        dtype = DTYPES[case % 3]
+        tdt = TORCH_DTYPE[dtype]
+        rows = int(rng.integers(1, 70))
+        h = int(rng.choice([int(rng.integers(1, 300)), int(rng.integers(300, 9000)), 4096, 4100, 8192]))
+        pad = int(rng.integers(0, 9))
+        off = int(rng.integers(0, 9))
+        what = f"case {case}: {dtype} rows={rows} h={h} pad={pad} off={off}"
+
+        def padded(width: int, start: int) -> torch.Tensor:
+            a = normal(rng, (rows * (width + pad) + 16,), 0, 1, dtype)  # room for any start <= 16
+            return _view(to_torch(a, dtype, cuda_device), rows, width, width + pad, start)
+
+        x = padded(h, off)
+        r = padded(h, off)
+        w = to_torch(normal(rng, (h,), 1, 0.1, dtype), dtype, cuda_device)
+        xn, rn, wn = to_numpy(x), to_numpy(r), to_numpy(w)
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+        y_ref, ro_ref = C.rmsnorm_residual(xn, rn, wn, 1e-5, dtype)
+        np.testing.assert_array_equal(to_numpy(ro), ro_ref, err_msg=what)
+        assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", what)
+        assert_parity(C.rmsnorm(xn, wn, 1e-6, dtype), to_numpy(kernels.rmsnorm_cuda_sm100(x, w, 1e-6)), dtype,
+                      "rmsnorm", what)
+
+        g, u = padded(h, off), padded(h, (off + 3) % 9)
+        assert_parity(C.swiglu(to_numpy(g), to_numpy(u), dtype), to_numpy(kernels.swiglu_cuda_sm100(g, u)), dtype,
+                      "swiglu", what)
+
+        d = 2 * int(rng.integers(1, 80))
+        heads, seq = int(rng.integers(1, 9)), int(rng.integers(1, 9))
+        style = O.ROPE_STYLES[case % 2]
+        qbase = to_torch(normal(rng, (seq * heads * (d + pad) + 16,), 0, 1, dtype), dtype, cuda_device)
+        q = qbase[off:].as_strided((1, seq, heads, d), (seq * heads * (d + pad), heads * (d + pad), d + pad, 1))
+        cos, sin = O.build_rope_tables(seq, d, offset=int(rng.integers(0, 100)))
+        yq = kernels.rope_cuda_sm100(q, to_torch(cos, O.F32, cuda_device), to_torch(sin, O.F32, cuda_device), style)
+        np.testing.assert_array_equal(to_numpy(yq), O.rope(to_numpy(q), cos, sin, style, dtype),
+                                      err_msg=f"{what} rope d={d} heads={heads} seq={seq} {style}")
