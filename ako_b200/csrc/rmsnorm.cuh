@@ -16,8 +16,9 @@
 //    TPR puts one row on a CTA (shuffle + one shared-memory exchange).
 //  * rms_generic_kernel: any width and alignment. One CTA per row, two
 //    passes (the second re-reads the row, an L2 hit for rows up to the L2
-//    size); 16-byte accesses for the part of each row where every operand is
-//    16-byte aligned, element accesses for the rest.
+//    size); when all of a row's pointers share one offset within 16 bytes,
+//    16-byte accesses for its aligned middle and element accesses for the
+//    ends, else element accesses throughout.
 #pragma once
 
 #include "common.cuh"
