@@ -46,6 +46,7 @@ import torch  # noqa: E402
 
 BF16_BYTES = 2
 FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e datasheet figure, the metric's "% of ~8 TB/s"
 L2_BYTES = 126 * 1024 * 1024
 
 WORKLOADS = {
@@ -400,6 +401,7 @@ def main() -> None:
             "frac": round(achieved / peak, 4),
             "traffic": traffic,
             "peak_source": peak_src,
+            "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
             "kernel": "ako_b200::rms_rows_kernel (CUDA events over the timed steps, launching stream)",
         },
         "cpu_baseline": cpu,
