@@ -37,14 +37,13 @@ bool use_staged(const RmsArgs& a, int es) {
 //    rows) keep enough loads in flight; wider rows keep 512-1024 threads with
 //    4 vectors each. Plain RMSNorm moves half as much per row and wants twice
 //    the vectors per thread with fewer threads (64-512 threads x 4, 512 x 8
-//    for 4096-vector rows), which also halves the per-warp fixed work. Rows
-//    wider than one CTA's registers hold (8192 vectors) are split over a
-//    cluster of 8.
+//    for 4096-vector fp32 rows), which also halves the per-warp fixed work.
+//    Fused rows of 4097-8192 vectors are split over a cluster of 8.
 //  * Few rows (decode): latency, not bandwidth, decides. One vector per
 //    thread (twice the threads) up to 512-vector rows; 2048-vector rows split
 //    over a cluster of 4 CTAs and 4096-vector rows over 4 or 8, so a row's
 //    loads come from several SMs at once.
-bool pick_shape(int64_t nvec, int64_t rows, bool residual, Shape* out) {
+bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
     const Shape& o = g_override;
     if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
         *out = o;
@@ -74,12 +73,25 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, Shape* out) {
                                   {1, 128, 4}, {1, 256, 4}, {1, 512, 4}, {1, 512, 8}};
     for (const Shape& s : residual ? fused : plain) {
         if (static_cast<int64_t>(s.tpr) * s.nv >= nvec) {
+            // 16-bit rows of 2049-4096 vectors: 512 x 8 needs 106 registers
+            // (one CTA per SM); 1024 x 4 streams 11% faster. fp32 keeps 512 x 8.
+            if (!residual && es == 2 && s.nv == 8) {
+                *out = Shape{1, 1024, 4};
+                return true;
+            }
             *out = s;
             return true;
         }
     }
     if (nvec <= 8192) {
-        *out = nvec % 8 == 0 ? Shape{8, 512, 2} : Shape{1, 1024, 8};
+        // Rows of 4097-8192 vectors: the fused form splits them over a cluster
+        // of 8 CTAs of 256 threads x 4 vectors (0.92 of peak, 0.76 with 512 x 2);
+        // plain rows stay in one CTA of 1024 threads x 8 vectors.
+        if (residual && nvec % 8 == 0) {
+            *out = Shape{8, 256, 4};
+            return true;
+        }
+        *out = Shape{1, 1024, 8};
         return true;
     }
     return false;
@@ -97,7 +109,7 @@ int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok) {
         constexpr int VEC = 16 / sizeof(T);
         Shape s;
-        if (pick_shape(a.h / VEC, a.rows, RES, &s)) {
+        if (pick_shape(a.h / VEC, a.rows, RES, static_cast<int>(sizeof(T)), &s)) {
             const int rc = launch_rms_rows<T, RES>(a, s.cluster, s.tpr, s.nv, st);
             if (rc >= 0) return rc;
         }
