@@ -25,7 +25,8 @@ __device__ int g_tma_status = 0;
 
 namespace {
 
-constexpr int kTmaThreads = 256;
+constexpr int kTmaThreads = 256;       // rows of up to 8 x 256 vectors
+constexpr int kTmaWideThreads = 1024;  // rows of up to 8 x 1024 vectors
 constexpr int kMaxStages = 8;
 constexpr uint32_t kWaitPolls = 1u << 24;   // ~a second of polling
 constexpr uint32_t kDrainPolls = 1u << 20;
@@ -36,10 +37,10 @@ struct TmaArgs {
     int stage_bytes;  // x row (+ residual row), multiple of 16
 };
 
-template <typename T, int NV, bool RES>
-__global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
+template <typename T, int NV, bool RES, int THREADS>
+__global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
     constexpr int VEC = 16 / sizeof(T);
-    constexpr int WARPS = kTmaThreads / 32;
+    constexpr int WARPS = THREADS / 32;
     using P = Packed<T, VEC>;
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ uint64_t full[kMaxStages];
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
         P v[NV];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            const int col = (j * THREADS + threadIdx.x) * VEC;
             if (col < h) v[j] = *reinterpret_cast<const P*>(xs + col);
         }
         if constexpr (RES) {
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
             T* ro = static_cast<T*>(a.ro) + row * a.sro;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
-                const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+                const int col = (j * THREADS + threadIdx.x) * VEC;
                 if (col < h) {
                     const P rv = *reinterpret_cast<const P*>(rs + col);
 #pragma unroll
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
         float part[NV];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            const int col = (j * THREADS + threadIdx.x) * VEC;
             float sq[VEC];
 #pragma unroll
             for (int e = 0; e < VEC; e += 2) {
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
         T* yr = static_cast<T*>(a.y) + row * a.sy;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int col = (j * kTmaThreads + threadIdx.x) * VEC;
+            const int col = (j * THREADS + threadIdx.x) * VEC;
             if (col < h) {
                 float w[VEC];
                 load_weight_vec<VEC>(a.w, a.wdtype, col, w);
@@ -164,12 +165,12 @@ __global__ void __launch_bounds__(kTmaThreads) rms_tma_kernel(const TmaArgs t) {
     }
 }
 
-template <typename T, int NV, bool RES>
+template <typename T, int NV, bool RES, int THREADS>
 int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
     const int row_bytes = a.h * static_cast<int>(sizeof(T));
     TmaArgs t{a, stages, RES ? 2 * row_bytes : row_bytes};
     const size_t smem = static_cast<size_t>(stages) * t.stage_bytes;
-    auto kernel = rms_tma_kernel<T, NV, RES>;
+    auto kernel = rms_tma_kernel<T, NV, RES, THREADS>;
     // Largest ring already allowed for this instantiation, per device.
     static int configured_bytes[64] = {0};
     int dev = 0;
@@ -184,19 +185,37 @@ int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
         }
         configured_bytes[dev] = static_cast<int>(smem);
     }
-    int64_t grid = static_cast<int64_t>(sm_count()) * ctas_per_sm;
+    // A persistent grid must be resident all at once: no more CTAs per SM than
+    // the registers, threads and shared memory allow.
+    int fit = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, kernel, THREADS, smem) != cudaSuccess || fit < 1) {
+        cudaGetLastError();
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm(staged): a %d-thread CTA with %zu bytes of shared memory does not fit an SM",
+                         THREADS, smem);
+    }
+    int64_t grid = static_cast<int64_t>(sm_count()) * (ctas_per_sm < fit ? ctas_per_sm : fit);
     if (grid > a.rows) grid = a.rows;
-    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), dim3(kTmaThreads), smem, 1, st, t,
+    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), dim3(THREADS), smem, 1, st, t,
                      RES ? "rmsnorm_residual(staged)" : "rmsnorm(staged)");
 }
 
 template <typename T, bool RES>
-int launch_dtype(const RmsArgs& a, int nv, int stages, int ctas_per_sm, cudaStream_t st) {
+int launch_dtype(const RmsArgs& a, int threads, int nv, int stages, int ctas_per_sm, cudaStream_t st) {
+    if (threads == kTmaWideThreads) {
+        switch (nv) {
+            case 4: return launch_one<T, 4, RES, kTmaWideThreads>(a, stages, ctas_per_sm, st);
+            case 8:
+                // Two rows of 8192 vectors exceed the ring's 200 KB.
+                if constexpr (RES) return -1;
+                else return launch_one<T, 8, RES, kTmaWideThreads>(a, stages, ctas_per_sm, st);
+            default: return -1;
+        }
+    }
     switch (nv) {
-        case 1: return launch_one<T, 1, RES>(a, stages, ctas_per_sm, st);
-        case 2: return launch_one<T, 2, RES>(a, stages, ctas_per_sm, st);
-        case 4: return launch_one<T, 4, RES>(a, stages, ctas_per_sm, st);
-        case 8: return launch_one<T, 8, RES>(a, stages, ctas_per_sm, st);
+        case 1: return launch_one<T, 1, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
+        case 2: return launch_one<T, 2, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
+        case 4: return launch_one<T, 4, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
+        case 8: return launch_one<T, 8, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
         default: return -1;
     }
 }
@@ -208,18 +227,21 @@ int launch_dtype(const RmsArgs& a, int nv, int stages, int ctas_per_sm, cudaStre
 int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st) {
     const int es = dtype_size(dtype);
     const int nvec = a.h * es / 16;
-    int nv = 1;
-    while (nv * kTmaThreads < nvec) nv *= 2;
+    // 256 threads up to 8 vectors each; wider rows take 1024 threads of 4 or 8.
+    int threads = kTmaThreads;
+    if (nvec > 8 * kTmaThreads) threads = kTmaWideThreads;
+    int nv = threads == kTmaThreads ? 1 : 4;
+    while (nv * threads < nvec) nv *= 2;
     if (nv > 8 || stages < 1 || stages > kMaxStages || ctas_per_sm < 1) return -1;
     const int row_bytes = a.h * es;
     if (static_cast<int64_t>(stages) * (res ? 2 : 1) * row_bytes > 200 * 1024) return -1;
     switch (dtype) {
-        case AKO_B200_F32: return res ? launch_dtype<float, true>(a, nv, stages, ctas_per_sm, st)
-                                      : launch_dtype<float, false>(a, nv, stages, ctas_per_sm, st);
-        case AKO_B200_F16: return res ? launch_dtype<__half, true>(a, nv, stages, ctas_per_sm, st)
-                                      : launch_dtype<__half, false>(a, nv, stages, ctas_per_sm, st);
-        default: return res ? launch_dtype<__nv_bfloat16, true>(a, nv, stages, ctas_per_sm, st)
-                            : launch_dtype<__nv_bfloat16, false>(a, nv, stages, ctas_per_sm, st);
+        case AKO_B200_F32: return res ? launch_dtype<float, true>(a, threads, nv, stages, ctas_per_sm, st)
+                                      : launch_dtype<float, false>(a, threads, nv, stages, ctas_per_sm, st);
+        case AKO_B200_F16: return res ? launch_dtype<__half, true>(a, threads, nv, stages, ctas_per_sm, st)
+                                      : launch_dtype<__half, false>(a, threads, nv, stages, ctas_per_sm, st);
+        default: return res ? launch_dtype<__nv_bfloat16, true>(a, threads, nv, stages, ctas_per_sm, st)
+                            : launch_dtype<__nv_bfloat16, false>(a, threads, nv, stages, ctas_per_sm, st);
     }
 }
 

@@ -197,6 +197,67 @@ def test_staged_rmsnorm_matches_oracle(cuda_device, dtype: str) -> None:
         lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
 
 
+def _kernel_names(fn) -> str:
+    """Names of the CUDA kernels ``fn`` launches, from torch's profiler."""
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return " ".join(e.name for e in prof.events())
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
+    """Rows of 2049-8192 vectors through the 1024-thread staged kernel: the
+    built-in choice for plain 16-bit rows of 16385-32768 elements from 2048
+    rows on, and forced for fp32, fused and 65536-wide rows. Its thread
+    layout is the row-resident kernel's (1024 threads x 4 or 8 vectors), so
+    the outputs are bit-identical to it; rows are checked against the oracle;
+    uneven rows per CTA, a strided view, and no bounded wait ran out."""
+    lib = _native.lib()
+    es = 4 if dtype == O.F32 else 2
+    tdt = TORCH_DTYPE[dtype]
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+
+    def rand(shape, mean=0.0, std=1.0):
+        return (torch.randn(shape, generator=g, device=cuda_device) * std + mean).to(tdt)
+
+    cases = [(2048, 16392, 0), (2051, 24576, 0), (2048, 32768, 0), (300, 32768, 2), (257, 65536 // (es // 2), 2)]
+    try:
+        for rows, h, mode in cases:
+            x, r, w = rand((rows, h)), rand((rows, h)), rand((h,), 1.0, 0.1)
+            forced = 1 if mode == 2 else 0  # one stage, one CTA per SM: the ring holds one wide row
+            assert lib.ako_b200_rmsnorm_set_staging(mode, forced, forced) == 0
+            y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+            if mode == 2 or (es == 2 and h > 16384):
+                assert "rms_tma_kernel" in _kernel_names(lambda: kernels.rmsnorm_cuda_sm100(x, w, 1e-6))
+            fused = h * es <= 65536  # two rows of the ring fit its 200 KB
+            if fused:
+                yr, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+            assert lib.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
+            assert torch.equal(y, kernels.rmsnorm_cuda_sm100(x, w, 1e-6)), (dtype, rows, h, mode)
+            if fused:
+                yr1, ro1 = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+                assert torch.equal(ro, ro1) and torch.equal(yr, yr1), (dtype, rows, h, mode)
+            sel = [0, 1, rows // 2, rows - 1]
+            xs, wn = to_numpy(x[sel]), to_numpy(w)
+            assert_parity(C.rmsnorm(xs, wn, 1e-6, dtype), to_numpy(y[sel]), dtype, "rmsnorm", f"wide h={h}")
+            if fused:
+                y_ref, ro_ref = C.rmsnorm_residual(xs, to_numpy(r[sel]), wn, 1e-5, dtype)
+                np.testing.assert_array_equal(to_numpy(ro[sel]), ro_ref)
+                assert_parity(y_ref, to_numpy(yr[sel]), dtype, "rmsnorm_residual", f"wide h={h}")
+        # a strided view through the built-in choice
+        assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
+        base = rand((2048, 32768 + 64))
+        xv, w = base[:, 64:], rand((32768,), 1.0, 0.1)
+        y = kernels.rmsnorm_cuda_sm100(xv, w, 1e-6)
+        assert_parity(C.rmsnorm(to_numpy(xv[:8]), to_numpy(w), 1e-6, dtype), to_numpy(y[:8]), dtype, "rmsnorm",
+                      "wide strided")
+        torch.cuda.synchronize()
+        assert _native.take_device_status() == 0
+    finally:
+        lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+
+
 def test_rmsnorm_leading_dims_and_empty(cuda_device) -> None:
     rng = np.random.default_rng(9)
     x = normal(rng, (2, 3, 5, 512), 0, 1, O.BF16)
@@ -365,6 +426,36 @@ def test_swiglu_packed_halves(cuda_device, dtype: str) -> None:
         y = kernels.swiglu_cuda_sm100(p[:, :f], p[:, f:])
         ref = C.swiglu(np.ascontiguousarray(packed[:, :f]), np.ascontiguousarray(packed[:, f:]), dtype)
         assert_parity(ref, to_numpy(y), dtype, "swiglu", f"packed {m}x{f}")
+
+
+@pytest.mark.parametrize("dtype", (O.F16, O.BF16))
+def test_swiglu_every_16bit_pattern(cuda_device, dtype: str) -> None:
+    """Every finite 16-bit pattern as the gate and as the up input (the other
+    operand kept where the product stays finite), against the oracle: covers
+    the kernel's conversions of subnormals, signed zeros and the largest
+    values; infinities and NaN give the oracle's classes."""
+    rng = np.random.default_rng(17)
+    bits = np.arange(65536, dtype=np.uint16)
+    exp_mask = 0x7C00 if dtype == O.F16 else 0x7F80
+    finite = bits[(bits & exp_mask) != exp_mask]
+    vals = finite.view(np.float16) if dtype == O.F16 else finite
+
+    def enc(a: np.ndarray) -> np.ndarray:
+        return O.encode(a.astype(np.float32), dtype) if dtype == O.BF16 else a.astype(np.float16)
+
+    n = vals.size
+    for g, u in ((vals, enc(rng.uniform(-0.9, 0.9, n))), (enc(rng.uniform(-1.0, 0.5, n)), vals)):
+        g2, u2 = g.reshape(1, n), u.reshape(1, n)
+        y = kernels.swiglu_cuda_sm100(to_torch(g2, dtype, cuda_device), to_torch(u2, dtype, cuda_device))
+        assert_parity(C.swiglu(g2, u2, dtype), to_numpy(y), dtype, "swiglu", "every pattern")
+    special = np.array([[np.inf, -np.inf, np.nan, 1.0, -1.0, 0.0, np.nan, 2.0]], dtype=np.float32)
+    ones = np.array([[1.0, 1.0, 1.0, np.inf, np.inf, np.inf, 1.0, np.nan]], dtype=np.float32)
+    gs, us = enc(special), enc(ones)
+    y = kernels.swiglu_cuda_sm100(to_torch(gs, dtype, cuda_device), to_torch(us, dtype, cuda_device))
+    ref = O.decode(C.swiglu(gs, us, dtype), dtype)
+    out = O.decode(to_numpy(y), dtype)
+    np.testing.assert_array_equal(np.isnan(out), np.isnan(ref))
+    np.testing.assert_array_equal(out[~np.isnan(ref)], ref[~np.isnan(ref)])
 
 
 def test_swiglu_extremes(cuda_device) -> None:
