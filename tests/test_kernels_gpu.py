@@ -406,7 +406,8 @@ def test_rope_position_zero_identity_and_empty(cuda_device) -> None:
 
 # ------------------------------------------------------------------ swiglu
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("shape", [(1, 5632), (64, 11008), (7, 100), (3, 14336), (2, 3, 8448), (1, 1), (33, 24)])
+@pytest.mark.parametrize("shape", [(1, 5632), (64, 11008), (7, 100), (3, 14336), (2, 3, 8448), (1, 1), (33, 24),
+                                   (2, 11008), (2, 16384), (1, 32776)])
 def test_swiglu_shapes(cuda_device, dtype: str, shape) -> None:
     rng = np.random.default_rng(sum(shape))
     g = normal(rng, shape, 0, 2, dtype)
