@@ -414,6 +414,10 @@ int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
 // (rmsnorm_tma.cu); -1 when the row is too wide for it.
 int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st);
 
+// Plain rows of 4097-8192 vectors streamed in two shared-memory chunks per
+// row (rmsnorm_tma.cu); -1 for other rows.
+int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st);
+
 // Reads and clears the staged kernels' device status word (synchronizing).
 int take_staged_status(int* status);
 

@@ -165,6 +165,168 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
     }
 }
 
+// Plain RMSNorm of rows of 4097-8192 vectors (16-bit rows of 32769-65536
+// elements, fp32 rows of 16385-32768), whose 1024 threads x 8 vectors do not
+// fit registers next to a next-row prefetch. Each row is two chunks of at
+// most 1024 x 4 vectors (64 KB), streamed through a ring of kChunkSlots
+// chunk slots by 1-D bulk copies: the chunks stay in shared memory, the sum
+// of squares reads them once and the output pass a second time, and each
+// slot is refilled with the chunk kChunkSlots ahead as soon as its output
+// is written, so the next row's chunks load while this row is finished.
+// Thread t owns vectors t + 1024 j (j = 0..7) as in rms_rows_kernel<T,
+// 1024, 8>, and the per-thread sum is the same pairwise tree split at its
+// middle, so the outputs are bit-identical to that kernel's.
+constexpr int kChunkSlots = 3;
+constexpr int kChunkNV = 4;  // vectors per thread per chunk
+
+struct ChunkArgs {
+    RmsArgs a;
+    int chunk_bytes;  // bytes of a full chunk (1024 x kChunkNV vectors)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const ChunkArgs c) {
+    constexpr int VEC = 16 / sizeof(T);
+    constexpr int THREADS = kTmaWideThreads;
+    constexpr int WARPS = THREADS / 32;
+    using P = Packed<T, VEC>;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ uint64_t full[kChunkSlots];
+    __shared__ float scratch[2][WARPS];
+    pdl_enter();
+    const RmsArgs& a = c.a;
+    const int h = a.h;
+    const uint32_t row_bytes = static_cast<uint32_t>(h) * sizeof(T);
+    const int64_t first = blockIdx.x;
+    const int64_t step = gridDim.x;
+    const int64_t my_rows = first < a.rows ? (a.rows - 1 - first) / step + 1 : 0;
+    const int64_t n_chunks = 2 * my_rows;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kChunkSlots; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // Chunk n of this CTA: half n % 2 of its row n / 2, into slot n % kChunkSlots.
+    auto issue = [&](int64_t n) {
+        const int64_t row = first + (n >> 1) * step;
+        const uint32_t off = (n & 1) ? static_cast<uint32_t>(c.chunk_bytes) : 0u;
+        const uint32_t bytes = (n & 1) ? row_bytes - off : static_cast<uint32_t>(c.chunk_bytes);
+        uint64_t* bar = &full[n % kChunkSlots];
+        mbar_expect_tx(bar, bytes);
+        bulk_load(ring + static_cast<size_t>(n % kChunkSlots) * c.chunk_bytes,
+                  reinterpret_cast<const unsigned char*>(static_cast<const T*>(a.x) + row * a.sx) + off, bytes, bar);
+    };
+    int64_t issued = 0;
+    if (threadIdx.x == 0) {
+        for (; issued < kChunkSlots && issued < n_chunks; ++issued) issue(issued);
+    }
+    // Waits for chunk n; on expiry records the status, lets every copy this
+    // CTA started land (bounded), and reports false to all threads.
+    auto arrive = [&](int64_t n) -> bool {
+        const bool ok = mbar_wait_bounded(&full[n % kChunkSlots], static_cast<uint32_t>(n / kChunkSlots) & 1u,
+                                          kWaitPolls);
+        if (!__syncthreads_or(!ok)) return true;
+        if (threadIdx.x == 0) {
+            atomicExch(&g_tma_status, kStatusWaitTimeout);
+            for (int64_t m = n; m < issued; ++m)
+                mbar_wait_bounded(&full[m % kChunkSlots], static_cast<uint32_t>(m / kChunkSlots) & 1u, kDrainPolls);
+        }
+        return false;
+    };
+
+    for (int64_t i = 0; i < my_rows; ++i) {
+        const int64_t row = first + i * step;
+        const int64_t n0 = 2 * i;
+        float half[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            if (!arrive(n0 + q)) return;
+            const T* xs = reinterpret_cast<const T*>(ring + static_cast<size_t>((n0 + q) % kChunkSlots) * c.chunk_bytes);
+            float part[kChunkNV];
+#pragma unroll
+            for (int j = 0; j < kChunkNV; ++j) {
+                const int v = j * THREADS + threadIdx.x;               // vector within the chunk
+                const int col = ((q * kChunkNV + j) * THREADS + threadIdx.x) * VEC;  // element within the row
+                float sq[VEC];
+                const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; e += 2) {
+                    const float2 f = get2<T, VEC>(xv, e);
+                    sq[e] = __fmul_rn(f.x, f.x);
+                    sq[e + 1] = __fmul_rn(f.y, f.y);
+                }
+                part[j] = col < h ? tree_sum<VEC>(sq) : 0.0f;
+            }
+            half[q] = tree_sum<kChunkNV>(part);
+        }
+        const float w_sum = warp_sum(__fadd_rn(half[0], half[1]));
+        float* sc = scratch[i & 1];
+        if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
+        __syncthreads();
+        float parts[WARPS];
+#pragma unroll
+        for (int k = 0; k < WARPS; ++k) parts[k] = sc[k];
+        const float inv = rms_inv(tree_sum<WARPS>(parts), a);
+        T* yr = static_cast<T*>(a.y) + row * a.sy;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int64_t n = n0 + q;
+            const T* xs = reinterpret_cast<const T*>(ring + static_cast<size_t>(n % kChunkSlots) * c.chunk_bytes);
+#pragma unroll
+            for (int j = 0; j < kChunkNV; ++j) {
+                const int v = j * THREADS + threadIdx.x;
+                const int col = ((q * kChunkNV + j) * THREADS + threadIdx.x) * VEC;
+                if (col < h) {
+                    const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
+                    float w[VEC];
+                    load_weight_vec<VEC>(a.w, a.wdtype, col, w);
+                    P o;
+#pragma unroll
+                    for (int e = 0; e < VEC; e += 2) {
+                        const float2 f = get2<T, VEC>(xv, e);
+                        put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w[e]),
+                                     __fmul_rn(__fmul_rn(f.y, inv), w[e + 1]));
+                    }
+                    st_global<T, VEC>(yr + col, o);
+                }
+            }
+            __syncthreads();  // every thread has read the slot
+            if (threadIdx.x == 0 && issued < n_chunks) {
+                fence_proxy_async_smem();
+                issue(issued);
+                ++issued;
+            }
+        }
+    }
+}
+
+template <typename T>
+int launch_chunked(const RmsArgs& a, cudaStream_t st) {
+    const int chunk_bytes = kTmaWideThreads * kChunkNV * 16;
+    ChunkArgs c{a, chunk_bytes};
+    const size_t smem = static_cast<size_t>(kChunkSlots) * chunk_bytes;
+    auto kernel = rms_chunk_kernel<T>;
+    static bool configured[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    if (!configured[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm(chunked): %zu bytes of shared memory: %s", smem,
+                             cudaGetErrorString(e));
+        }
+        configured[dev] = true;
+    }
+    int64_t grid = sm_count();
+    if (grid > a.rows) grid = a.rows;
+    return launch_ex(kernel, dim3(static_cast<unsigned>(grid)), dim3(kTmaWideThreads), smem, 1, st, c,
+                     "rmsnorm(chunked)");
+}
+
 template <typename T, int NV, bool RES, int THREADS>
 int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
     const int row_bytes = a.h * static_cast<int>(sizeof(T));
@@ -242,6 +404,20 @@ int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int cta
                                       : launch_dtype<__half, false>(a, threads, nv, stages, ctas_per_sm, st);
         default: return res ? launch_dtype<__nv_bfloat16, true>(a, threads, nv, stages, ctas_per_sm, st)
                             : launch_dtype<__nv_bfloat16, false>(a, threads, nv, stages, ctas_per_sm, st);
+    }
+}
+
+// Chunked launch for plain rows of 4097-8192 16-byte vectors (16-byte aligned
+// rows); -1 for other rows.
+int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st) {
+    const int es = dtype_size(dtype);
+    const int64_t nvec = static_cast<int64_t>(a.h) * es / 16;
+    const int64_t per_chunk = static_cast<int64_t>(kTmaWideThreads) * kChunkNV;
+    if (nvec <= per_chunk || nvec > 2 * per_chunk) return -1;
+    switch (dtype) {
+        case AKO_B200_F32: return launch_chunked<float>(a, st);
+        case AKO_B200_F16: return launch_chunked<__half>(a, st);
+        default: return launch_chunked<__nv_bfloat16>(a, st);
     }
 }
 

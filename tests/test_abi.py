@@ -169,6 +169,8 @@ def test_multiply_high_division_is_exact(d: int) -> None:
 def test_staging_hook_validation(lib) -> None:
     assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
     assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 1
+    assert lib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
+    assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
+    assert lib.ako_b200_rmsnorm_set_staging(4, 0, 0) == 1
     assert lib.ako_b200_rmsnorm_set_staging(2, 9, 1) == 1
     assert lib.ako_b200_take_device_status(None) == 1

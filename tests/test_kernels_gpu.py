@@ -207,12 +207,14 @@ def _kernel_names(fn) -> str:
 
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
-    """Rows of 2049-8192 vectors through the 1024-thread staged kernel: the
+    """Rows of 2049-8192 vectors through the 1024-thread staged kernel (the
     built-in choice for plain 16-bit rows of 16385-32768 elements from 2048
-    rows on, and forced for fp32, fused and 65536-wide rows. Its thread
-    layout is the row-resident kernel's (1024 threads x 4 or 8 vectors), so
-    the outputs are bit-identical to it; rows are checked against the oracle;
-    uneven rows per CTA, a strided view, and no bounded wait ran out."""
+    rows on; forced for fp32, fused and 65536-wide rows) and through the
+    chunked kernel (plain rows of 4097-8192 vectors, full and partial second
+    chunks). Both keep the row-resident kernel's thread layout (1024 threads
+    x 4 or 8 vectors) and sums, so the outputs are bit-identical to it; rows
+    are checked against the oracle; uneven rows per CTA, a strided view, and
+    no bounded wait ran out."""
     lib = _native.lib()
     es = 4 if dtype == O.F32 else 2
     tdt = TORCH_DTYPE[dtype]
@@ -221,15 +223,23 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
     def rand(shape, mean=0.0, std=1.0):
         return (torch.randn(shape, generator=g, device=cuda_device) * std + mean).to(tdt)
 
-    cases = [(2048, 16392, 0), (2051, 24576, 0), (2048, 32768, 0), (300, 32768, 2), (257, 65536 // (es // 2), 2)]
+    wide = 65536 // (es // 2) if es != 4 else 32768  # 8192 vectors
+    cases = [(2048, 16392, 0), (2051, 24576, 0), (2048, 32768, 0), (300, 32768, 2), (257, wide, 2),
+             (257, wide, 3), (300, wide - 8 // (es // 2) if es == 2 else wide - 4, 3), (150, 40968 // (es // 2), 3),
+             (512, wide, 0)]
     try:
         for rows, h, mode in cases:
             x, r, w = rand((rows, h)), rand((rows, h)), rand((h,), 1.0, 0.1)
             forced = 1 if mode == 2 else 0  # one stage, one CTA per SM: the ring holds one wide row
             assert lib.ako_b200_rmsnorm_set_staging(mode, forced, forced) == 0
             y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
-            if mode == 2 or (es == 2 and h > 16384):
-                assert "rms_tma_kernel" in _kernel_names(lambda: kernels.rmsnorm_cuda_sm100(x, w, 1e-6))
+            expect = {2: "rms_tma_kernel", 3: "rms_chunk_kernel"}.get(mode)
+            if mode == 0 and es == 2 and 16384 < h <= 32768 and rows >= 2048:
+                expect = "rms_tma_kernel"
+            if mode == 0 and es == 2 and h > 32768 and rows >= 128:
+                expect = "rms_chunk_kernel"
+            if expect:
+                assert expect in _kernel_names(lambda: kernels.rmsnorm_cuda_sm100(x, w, 1e-6)), (dtype, rows, h, mode)
             fused = h * es <= 65536  # two rows of the ring fit its 200 KB
             if fused:
                 yr, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
