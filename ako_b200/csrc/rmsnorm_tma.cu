@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     const int64_t step = gridDim.x;
     const int64_t my_rows = first < a.rows ? (a.rows - 1 - first) / step + 1 : 0;
     const int64_t n_chunks = 2 * my_rows;
+    const bool w_same = a.wdtype == dtype_code<T>();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kChunkSlots; ++s) mbar_init(&full[s], 1);
@@ -261,6 +262,18 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
             }
             half[q] = tree_sum<kChunkNV>(part);
         }
+        // Weights of the first chunk, loaded while the row's sum is reduced
+        // (when they have the row's dtype; other weights load at use).
+        P wpre[kChunkNV];
+        auto prefetch_w = [&](int q) {
+            if (!w_same) return;
+#pragma unroll
+            for (int j = 0; j < kChunkNV; ++j) {
+                const int col = ((q * kChunkNV + j) * THREADS + threadIdx.x) * VEC;
+                if (col < h) wpre[j] = ld_cached<T, VEC>(static_cast<const T*>(a.w) + col);
+            }
+        };
+        prefetch_w(0);
         const float w_sum = warp_sum(__fadd_rn(half[0], half[1]));
         float* sc = scratch[i & 1];
         if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
@@ -281,7 +294,16 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
                 if (col < h) {
                     const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
                     float w[VEC];
-                    load_weight_vec<VEC>(a.w, a.wdtype, col, w);
+                    if (w_same) {
+#pragma unroll
+                        for (int e = 0; e < VEC; e += 2) {
+                            const float2 wf = get2<T, VEC>(wpre[j], e);
+                            w[e] = wf.x;
+                            w[e + 1] = wf.y;
+                        }
+                    } else {
+                        load_weight_vec<VEC>(a.w, a.wdtype, col, w);
+                    }
                     P o;
 #pragma unroll
                     for (int e = 0; e < VEC; e += 2) {
@@ -292,6 +314,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
                     st_global<T, VEC>(yr + col, o);
                 }
             }
+            if (q == 0) prefetch_w(1);
             __syncthreads();  // every thread has read the slot
             if (threadIdx.x == 0 && issued < n_chunks) {
                 fence_proxy_async_smem();

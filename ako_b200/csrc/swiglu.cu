@@ -128,8 +128,8 @@ __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
                 if constexpr (VEC % 2 == 0) {
 #pragma unroll
                     for (int e = 0; e < VEC; e += 2) {
-                        const float2 gf = get2<T, VEC>(g[k], e);
-                        const float2 uf = get2<T, VEC>(u[k], e);
+                        const float2 gf = get2_cvt<T, VEC>(g[k], e);
+                        const float2 uf = get2_cvt<T, VEC>(u[k], e);
                         put2<T, VEC>(o, e, silu_mul<T>(gf.x, uf.x), silu_mul<T>(gf.y, uf.y));
                     }
                 } else {
