@@ -1,6 +1,6 @@
 """Plain RMSNorm on rows wider than the benchmark's (16385-65536 elements):
 the row-resident kernel against the built-in choice, which sends plain 16-bit
-rows of 16385-32768 elements (from 2048 rows) to the staged kernel and of
+rows of 16385-32768 elements (from 1024 rows) to the staged kernel and of
 32769-65536 elements (from 128 rows) to the chunked kernel.
 
     python -m ako_b200.benchmark.wide_rows            # timing table

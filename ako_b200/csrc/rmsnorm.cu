@@ -16,13 +16,13 @@ Shape g_override = {0, 0, 0};
 
 // Staging mode: 0 = built-in choice, 1 = row-resident kernel only,
 // 2 = staged (bulk-copy ring) kernel where it applies, 3 = chunked kernel
-// where it applies (plain rows of 4097-8192 vectors).
+// where it applies (plain rows of 2049-8192 vectors).
 int g_mode = 0;
 int g_stages = 0;
 int g_ctas_per_sm = 0;
 
 // Rows from which plain 16-bit rows of 2049-4096 vectors take the staged kernel.
-constexpr int64_t kStagedMinRows = 2048;
+constexpr int64_t kStagedMinRows = 1024;
 // Rows from which plain 16-bit rows of 4097-8192 vectors take the chunked
 // kernel (measured faster from 148 rows, one per SM, up).
 constexpr int64_t kChunkedMinRows = 128;
@@ -32,9 +32,10 @@ constexpr int64_t kChunkedMinRows = 128;
 // x 4 vectors in registers, one CTA per SM, so a row's reduction and stores
 // leave HBM idle for that SM; the staged kernel with the same thread layout
 // loads the next row into shared memory meanwhile (one stage, one CTA per
-// SM): 0.87 against 0.75 of peak at 8192 x 32768 bf16, bit-identical output.
-// With few rows per SM the persistent grid's start-up costs more than it
-// saves. Other shapes keep the row-resident kernel, which measured equal or
+// SM): 0.92 against 0.75 of peak at 8192 x 32768 bf16, bit-identical output.
+// Below ~1024 rows (7 per SM) the persistent grid's start-up costs about
+// what it saves. The chunked kernel with one chunk per row (the row held in
+// shared memory instead of registers) measured level with this one. Other shapes keep the row-resident kernel, which measured equal or
 // faster (fp32, fused residual, 65536-wide rows).
 bool use_staged(const RmsArgs& a, int es, bool res) {
     if (g_mode == 1 || g_mode == 3) return false;

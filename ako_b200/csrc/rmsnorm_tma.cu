@@ -165,17 +165,20 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
     }
 }
 
-// Plain RMSNorm of rows of 4097-8192 vectors (16-bit rows of 32769-65536
-// elements, fp32 rows of 16385-32768), whose 1024 threads x 8 vectors do not
-// fit registers next to a next-row prefetch. Each row is two chunks of at
-// most 1024 x 4 vectors (64 KB), streamed through a ring of kChunkSlots
-// chunk slots by 1-D bulk copies: the chunks stay in shared memory, the sum
-// of squares reads them once and the output pass a second time, and each
-// slot is refilled with the chunk kChunkSlots ahead as soon as its output
-// is written, so the next row's chunks load while this row is finished.
-// Thread t owns vectors t + 1024 j (j = 0..7) as in rms_rows_kernel<T,
-// 1024, 8>, and the per-thread sum is the same pairwise tree split at its
-// middle, so the outputs are bit-identical to that kernel's.
+// Plain RMSNorm of rows of 2049-8192 vectors, CHUNKS = 1 (up to 4096) or 2
+// chunks of at most 1024 x 4 vectors (64 KB) per row. Built for the rows of
+// 4097-8192 vectors (16-bit rows of 32769-65536 elements, fp32 of
+// 16385-32768), whose 1024 threads x 8 vectors do not fit registers next to
+// a next-row prefetch. The chunks stream through a ring of kChunkSlots
+// shared-memory slots by 1-D bulk copies and stay there: the sum of squares
+// reads them once and the output pass a second time, and each slot is
+// refilled with the chunk kChunkSlots ahead as soon as its outputs are
+// written, so the next row loads while this one is finished. A chunk's
+// weights (when they have the row's dtype) are loaded into registers while
+// the row's sum is reduced, or while the previous chunk is written. Thread t
+// owns vectors t + 1024 j as in rms_rows_kernel<T, 1024, 4 * CHUNKS>, and
+// the per-thread sum is the same pairwise tree split between the chunks, so
+// the outputs are bit-identical to that kernel's.
 constexpr int kChunkSlots = 3;
 constexpr int kChunkNV = 4;  // vectors per thread per chunk
 
@@ -184,7 +187,7 @@ struct ChunkArgs {
     int chunk_bytes;  // bytes of a full chunk (1024 x kChunkNV vectors)
 };
 
-template <typename T>
+template <typename T, int CHUNKS>
 __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const ChunkArgs c) {
     constexpr int VEC = 16 / sizeof(T);
     constexpr int THREADS = kTmaWideThreads;
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     const int64_t first = blockIdx.x;
     const int64_t step = gridDim.x;
     const int64_t my_rows = first < a.rows ? (a.rows - 1 - first) / step + 1 : 0;
-    const int64_t n_chunks = 2 * my_rows;
+    const int64_t n_chunks = CHUNKS * my_rows;
     const bool w_same = a.wdtype == dtype_code<T>();
 
     if (threadIdx.x == 0) {
@@ -209,11 +212,13 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     }
     __syncthreads();
 
-    // Chunk n of this CTA: half n % 2 of its row n / 2, into slot n % kChunkSlots.
+    // Chunk n of this CTA: part n % CHUNKS of its row n / CHUNKS, into slot
+    // n % kChunkSlots; the last part takes the rest of the row.
     auto issue = [&](int64_t n) {
-        const int64_t row = first + (n >> 1) * step;
-        const uint32_t off = (n & 1) ? static_cast<uint32_t>(c.chunk_bytes) : 0u;
-        const uint32_t bytes = (n & 1) ? row_bytes - off : static_cast<uint32_t>(c.chunk_bytes);
+        const int64_t row = first + (n / CHUNKS) * step;
+        const int part = static_cast<int>(n % CHUNKS);
+        const uint32_t off = static_cast<uint32_t>(part) * static_cast<uint32_t>(c.chunk_bytes);
+        const uint32_t bytes = part == CHUNKS - 1 ? row_bytes - off : static_cast<uint32_t>(c.chunk_bytes);
         uint64_t* bar = &full[n % kChunkSlots];
         mbar_expect_tx(bar, bytes);
         bulk_load(ring + static_cast<size_t>(n % kChunkSlots) * c.chunk_bytes,
@@ -239,10 +244,10 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
 
     for (int64_t i = 0; i < my_rows; ++i) {
         const int64_t row = first + i * step;
-        const int64_t n0 = 2 * i;
-        float half[2];
+        const int64_t n0 = CHUNKS * i;
+        float half[CHUNKS];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < CHUNKS; ++q) {
             if (!arrive(n0 + q)) return;
             const T* xs = reinterpret_cast<const T*>(ring + static_cast<size_t>((n0 + q) % kChunkSlots) * c.chunk_bytes);
             float part[kChunkNV];
@@ -250,15 +255,18 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
             for (int j = 0; j < kChunkNV; ++j) {
                 const int v = j * THREADS + threadIdx.x;               // vector within the chunk
                 const int col = ((q * kChunkNV + j) * THREADS + threadIdx.x) * VEC;  // element within the row
-                float sq[VEC];
-                const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
+                part[j] = 0.0f;
+                if (col < h) {  // a slot holds only its chunk's bytes
+                    float sq[VEC];
+                    const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
 #pragma unroll
-                for (int e = 0; e < VEC; e += 2) {
-                    const float2 f = get2<T, VEC>(xv, e);
-                    sq[e] = __fmul_rn(f.x, f.x);
-                    sq[e + 1] = __fmul_rn(f.y, f.y);
+                    for (int e = 0; e < VEC; e += 2) {
+                        const float2 f = get2<T, VEC>(xv, e);
+                        sq[e] = __fmul_rn(f.x, f.x);
+                        sq[e + 1] = __fmul_rn(f.y, f.y);
+                    }
+                    part[j] = tree_sum<VEC>(sq);
                 }
-                part[j] = col < h ? tree_sum<VEC>(sq) : 0.0f;
             }
             half[q] = tree_sum<kChunkNV>(part);
         }
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
             }
         };
         prefetch_w(0);
-        const float w_sum = warp_sum(__fadd_rn(half[0], half[1]));
+        const float w_sum = warp_sum(CHUNKS == 2 ? __fadd_rn(half[0], half[CHUNKS - 1]) : half[0]);
         float* sc = scratch[i & 1];
         if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
         __syncthreads();
@@ -284,7 +292,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
         const float inv = rms_inv(tree_sum<WARPS>(parts), a);
         T* yr = static_cast<T*>(a.y) + row * a.sy;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < CHUNKS; ++q) {
             const int64_t n = n0 + q;
             const T* xs = reinterpret_cast<const T*>(ring + static_cast<size_t>(n % kChunkSlots) * c.chunk_bytes);
 #pragma unroll
@@ -314,7 +322,7 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
                     st_global<T, VEC>(yr + col, o);
                 }
             }
-            if (q == 0) prefetch_w(1);
+            if (q + 1 < CHUNKS) prefetch_w(q + 1);
             __syncthreads();  // every thread has read the slot
             if (threadIdx.x == 0 && issued < n_chunks) {
                 fence_proxy_async_smem();
@@ -325,16 +333,19 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     }
 }
 
-template <typename T>
+template <typename T, int CHUNKS>
 int launch_chunked(const RmsArgs& a, cudaStream_t st) {
-    const int chunk_bytes = kTmaWideThreads * kChunkNV * 16;
+    // One-chunk rows get slots of their own size, which leaves the rest of
+    // the SM's shared memory to L1 (the weight stays there).
+    const int chunk_bytes = CHUNKS == 1 ? a.h * static_cast<int>(sizeof(T)) : kTmaWideThreads * kChunkNV * 16;
     ChunkArgs c{a, chunk_bytes};
     const size_t smem = static_cast<size_t>(kChunkSlots) * chunk_bytes;
-    auto kernel = rms_chunk_kernel<T>;
-    static bool configured[64] = {false};
+    auto kernel = rms_chunk_kernel<T, CHUNKS>;
+    // Largest ring already allowed for this instantiation, per device.
+    static size_t configured[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-    if (!configured[dev]) {
+    if (smem > configured[dev]) {
         const cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) {
@@ -342,7 +353,7 @@ int launch_chunked(const RmsArgs& a, cudaStream_t st) {
             return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm(chunked): %zu bytes of shared memory: %s", smem,
                              cudaGetErrorString(e));
         }
-        configured[dev] = true;
+        configured[dev] = smem;
     }
     int64_t grid = sm_count();
     if (grid > a.rows) grid = a.rows;
@@ -430,17 +441,18 @@ int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int cta
     }
 }
 
-// Chunked launch for plain rows of 4097-8192 16-byte vectors (16-byte aligned
-// rows); -1 for other rows.
+// Chunked launch for plain rows of 2049-8192 16-byte vectors (16-byte aligned
+// rows): one chunk per row up to 4096 vectors, two above; -1 for other rows.
 int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st) {
     const int es = dtype_size(dtype);
     const int64_t nvec = static_cast<int64_t>(a.h) * es / 16;
     const int64_t per_chunk = static_cast<int64_t>(kTmaWideThreads) * kChunkNV;
-    if (nvec <= per_chunk || nvec > 2 * per_chunk) return -1;
+    if (nvec <= per_chunk / 2 || nvec > 2 * per_chunk) return -1;
+    const bool two = nvec > per_chunk;
     switch (dtype) {
-        case AKO_B200_F32: return launch_chunked<float>(a, st);
-        case AKO_B200_F16: return launch_chunked<__half>(a, st);
-        default: return launch_chunked<__nv_bfloat16>(a, st);
+        case AKO_B200_F32: return two ? launch_chunked<float, 2>(a, st) : launch_chunked<float, 1>(a, st);
+        case AKO_B200_F16: return two ? launch_chunked<__half, 2>(a, st) : launch_chunked<__half, 1>(a, st);
+        default: return two ? launch_chunked<__nv_bfloat16, 2>(a, st) : launch_chunked<__nv_bfloat16, 1>(a, st);
     }
 }
 

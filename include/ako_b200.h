@@ -178,8 +178,8 @@ int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_pe
  * row-resident kernel only; mode 2 uses, where the row fits, the persistent
  * kernel that stages rows in shared memory with 1-D bulk copies (`stages`
  * rows in flight per CTA, `ctas_per_sm` CTAs per SM; 0 = defaults); mode 3
- * uses, for plain rows of 4097-8192 16-byte vectors, the persistent kernel
- * that streams each row through shared memory in two chunks; mode 0
+ * uses, for plain rows of 2049-8192 16-byte vectors, the persistent kernel
+ * that streams each row through shared memory in one or two chunks; mode 0
  * restores the built-in choice. Not part of the reference's interface; it
  * has no counterpart there. Process-wide, not thread-safe.
  */

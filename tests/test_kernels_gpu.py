@@ -208,7 +208,7 @@ def _kernel_names(fn) -> str:
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
     """Rows of 2049-8192 vectors through the 1024-thread staged kernel (the
-    built-in choice for plain 16-bit rows of 16385-32768 elements from 2048
+    built-in choice for plain 16-bit rows of 16385-32768 elements from 1024
     rows on; forced for fp32, fused and 65536-wide rows) and through the
     chunked kernel (plain rows of 4097-8192 vectors, full and partial second
     chunks). Both keep the row-resident kernel's thread layout (1024 threads
@@ -227,6 +227,8 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
     cases = [(2048, 16392, 0), (2051, 24576, 0), (2048, 32768, 0), (300, 32768, 2), (257, wide, 2),
              (257, wide, 3), (300, wide - 8 // (es // 2) if es == 2 else wide - 4, 3), (150, 40968 // (es // 2), 3),
              (512, wide, 0)]
+    if es == 2:  # one chunk per row: the row-resident kernel has the same 1024 x 4 layout
+        cases += [(300, 32768, 3), (257, 24584, 3), (2049, 16392, 3)]
     try:
         for rows, h, mode in cases:
             x, r, w = rand((rows, h)), rand((rows, h)), rand((h,), 1.0, 0.1)
@@ -234,7 +236,7 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
             assert lib.ako_b200_rmsnorm_set_staging(mode, forced, forced) == 0
             y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
             expect = {2: "rms_tma_kernel", 3: "rms_chunk_kernel"}.get(mode)
-            if mode == 0 and es == 2 and 16384 < h <= 32768 and rows >= 2048:
+            if mode == 0 and es == 2 and 16384 < h <= 32768 and rows >= 1024:
                 expect = "rms_tma_kernel"
             if mode == 0 and es == 2 and h > 32768 and rows >= 128:
                 expect = "rms_chunk_kernel"
