@@ -1,7 +1,7 @@
 """Plain RMSNorm on rows wider than the benchmark's (16385-65536 elements):
 the row-resident kernel against the built-in choice, which sends plain 16-bit
 rows of 16385-32768 elements (from 1024 rows) to the staged kernel and of
-32769-65536 elements (from 128 rows) to the chunked kernel.
+32769-65536 elements (fp16 from 128 rows, bf16 from 1024) to the chunked kernel.
 
     python -m ako_b200.benchmark.wide_rows            # timing table
     python -m ako_b200.benchmark.wide_rows --capture  # one launch of each wide-row kernel, for ncu
@@ -28,8 +28,8 @@ from ako_b200.benchmark.timing import Flusher, cold_us
 
 CELLS = (
     ("bf16", 2048, 32768), ("bf16", 8192, 32768), ("fp16", 16384, 24576), ("bf16", 1024, 32768),
-    ("bf16", 148, 65528), ("bf16", 2048, 65536), ("bf16", 8192, 65536), ("fp16", 8192, 65536),
-    ("bf16", 8192, 40960), ("fp32", 8192, 32768),
+    ("bf16", 148, 65528), ("fp16", 148, 65536), ("bf16", 1024, 65536), ("bf16", 2048, 65536),
+    ("bf16", 8192, 65536), ("fp16", 8192, 65536), ("bf16", 8192, 40960), ("fp32", 8192, 32768),
 )
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 

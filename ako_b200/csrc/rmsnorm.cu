@@ -24,8 +24,11 @@ int g_ctas_per_sm = 0;
 // Rows from which plain 16-bit rows of 2049-4096 vectors take the staged kernel.
 constexpr int64_t kStagedMinRows = 1024;
 // Rows from which plain 16-bit rows of 4097-8192 vectors take the chunked
-// kernel (measured faster from 148 rows, one per SM, up).
-constexpr int64_t kChunkedMinRows = 128;
+// kernel: fp16 from 148 rows (one per SM) up measured faster; bf16, whose
+// row-resident kernel widens by shift and mask, was slower at 148 rows and
+// faster from 2048.
+constexpr int64_t kChunkedMinRowsF16 = 128;
+constexpr int64_t kChunkedMinRowsBF16 = 1024;
 
 // Built-in choice between the row-resident and the staged kernel. Plain
 // 16-bit rows of 2049-4096 vectors (16385-32768 elements) need 1024 threads
@@ -47,14 +50,15 @@ bool use_staged(const RmsArgs& a, int es, bool res) {
 // Built-in choice of the chunked kernel: plain 16-bit rows of 4097-8192
 // vectors (32769-65536 elements). The row-resident 1024 x 8 CTA is alone on
 // its SM and idles HBM while it reduces and stores a row; the chunked kernel
-// streams the next row meanwhile, with the same sums and outputs:
-// 0.56-0.71 -> 0.77-0.86 of peak at 8192 rows, 15-35% faster from 148 rows
-// up. fp32 rows of that many vectors measured level or slower chunked.
-bool use_chunked(const RmsArgs& a, int es) {
+// streams the next row meanwhile, with the same sums and outputs (8192 x
+// 65536: fp16 0.71 -> 0.93 of peak, bf16 0.83 -> 0.90). fp32 rows of that
+// many vectors measured level or slower chunked.
+bool use_chunked(const RmsArgs& a, int dtype) {
     if (g_mode == 3) return true;
-    if (g_mode != 0 || g_override.tpr != 0) return false;
-    const int64_t nvec = static_cast<int64_t>(a.h) * es / 16;
-    return es == 2 && nvec > 4096 && nvec <= 8192 && a.rows >= kChunkedMinRows;
+    if (g_mode != 0 || g_override.tpr != 0 || dtype == AKO_B200_F32) return false;
+    const int64_t nvec = static_cast<int64_t>(a.h) * 2 / 16;
+    const int64_t min_rows = dtype == AKO_B200_F16 ? kChunkedMinRowsF16 : kChunkedMinRowsBF16;
+    return nvec > 4096 && nvec <= 8192 && a.rows >= min_rows;
 }
 
 // Launch shape for `rows` rows of `nvec` 16-byte vectors, from sweeps of
@@ -127,7 +131,7 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
 
 template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
-    if (vector_ok && !RES && use_chunked(a, sizeof(T))) {
+    if (vector_ok && !RES && use_chunked(a, dtype_code<T>())) {
         const int rc = launch_rms_chunked(a, dtype_code<T>(), st);
         if (rc >= 0) return rc;
     }

@@ -238,7 +238,7 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
             expect = {2: "rms_tma_kernel", 3: "rms_chunk_kernel"}.get(mode)
             if mode == 0 and es == 2 and 16384 < h <= 32768 and rows >= 1024:
                 expect = "rms_tma_kernel"
-            if mode == 0 and es == 2 and h > 32768 and rows >= 128:
+            if mode == 0 and es == 2 and h > 32768 and rows >= (128 if dtype == O.F16 else 1024):
                 expect = "rms_chunk_kernel"
             if expect:
                 assert expect in _kernel_names(lambda: kernels.rmsnorm_cuda_sm100(x, w, 1e-6)), (dtype, rows, h, mode)
