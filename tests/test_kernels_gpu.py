@@ -281,6 +281,49 @@ def test_rmsnorm_leading_dims_and_empty(cuda_device) -> None:
     assert kernels.rmsnorm_cuda_sm100(empty, to_torch(w, O.BF16, cuda_device)).shape == (0, 512)
 
 
+def test_offsets_beyond_2_31_elements(cuda_device) -> None:
+    """Tensors of more than 2^31 elements (4.3 GB in bf16): every op's last
+    rows sit past any 32-bit element offset. Their outputs, and the first
+    rows', match the oracle (a wrapped offset would write the wrong rows)."""
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    bf = torch.bfloat16
+
+    def rand(*shape):
+        return torch.randn(*shape, generator=g, device=cuda_device).to(bf)
+
+    def ends(t):
+        return torch.cat([t[:2], t[-3:]])
+
+    h = 4096
+    rows = (1 << 31) // h + 3
+    x, r, w = rand(rows, h), rand(rows, h), rand(h)
+    y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+    y_ref, ro_ref = C.rmsnorm_residual(to_numpy(ends(x)), to_numpy(ends(r)), to_numpy(w), 1e-5, O.BF16)
+    np.testing.assert_array_equal(to_numpy(ends(ro)), ro_ref)
+    assert_parity(y_ref, to_numpy(ends(y)), O.BF16, "rmsnorm_residual", "beyond 2^31")
+    del r, ro, y
+    y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+    assert_parity(C.rmsnorm(to_numpy(ends(x)), to_numpy(w), 1e-6, O.BF16), to_numpy(ends(y)), O.BF16, "rmsnorm",
+                  "beyond 2^31")
+    del x, y
+
+    f = 14336
+    m = (1 << 31) // f + 3
+    gate, up = rand(m, f) * 2, rand(m, f) * 2
+    y = kernels.swiglu_cuda_sm100(gate, up)
+    assert_parity(C.swiglu(to_numpy(ends(gate)), to_numpy(ends(up)), O.BF16), to_numpy(ends(y)), O.BF16, "swiglu",
+                  "beyond 2^31")
+    del gate, up, y
+
+    s = (1 << 31) // (32 * 128) + 2
+    q = rand(1, s, 32, 128)
+    cos, sin = (torch.from_numpy(t).to(cuda_device) for t in O.build_rope_tables(s, 128))
+    y = kernels.rope_cuda_sm100(q, cos, sin, "neox")
+    for lo, hi in ((0, 2), (s - 2, s)):
+        ref = C.rope(to_numpy(q[:, lo:hi]), to_numpy(cos[lo:hi]), to_numpy(sin[lo:hi]), "neox", O.BF16)
+        np.testing.assert_array_equal(to_numpy(y[:, lo:hi]), ref)
+
+
 def test_rmsnorm_rejects_oversized_hidden_dim(cuda_device) -> None:
     x = torch.randn(1, kernels.MAX_HIDDEN_DIM + 2, device=cuda_device)
     with pytest.raises(ValueError, match="hidden_dim"):
