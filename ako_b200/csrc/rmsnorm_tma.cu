@@ -1,16 +1,22 @@
-// RMSNorm / fused residual RMSNorm with rows staged in shared memory by 1-D
-// bulk copies (cp.async.bulk, mbarrier completion): a persistent kernel for
-// row counts too small to keep HBM busy with one short-lived CTA per row.
+// Persistent RMSNorm kernels fed by 1-D bulk copies into shared memory
+// (cp.async.bulk, mbarrier completion, no multicast), for rows whose
+// row-resident CTA sits alone on its SM and leaves HBM idle while it reduces
+// and stores a row.
 //
-// Each CTA owns rows blockIdx.x, blockIdx.x + gridDim.x, ... and a ring of
-// `stages` shared-memory slots. Thread 0 keeps up to `stages` rows in flight
-// (x, and the residual when fused); all threads wait on the slot's mbarrier,
-// read their 16-byte vectors into registers, and the slot is refilled with
-// the row `stages` ahead as soon as the reduction's barrier shows every
-// thread has read it. Arithmetic and rounding are those of rms_rows_kernel;
-// the pairwise sum of squares is partitioned over 256 threads, so fp32
-// results can differ from a row-resident launch of another thread count in
-// the last bits (the rounded residual is identical).
+// rms_tma_kernel (plain and fused): each CTA owns rows blockIdx.x,
+// blockIdx.x + gridDim.x, ... and a ring of `stages` shared-memory slots.
+// Thread 0 keeps up to `stages` rows in flight (x, and the residual when
+// fused); all threads wait on the slot's mbarrier, read their 16-byte
+// vectors into registers, and the slot is refilled with the row `stages`
+// ahead as soon as the reduction's barrier shows every thread has read it.
+// Arithmetic and rounding are those of rms_rows_kernel; the pairwise sum of
+// squares is partitioned over THREADS threads (256, or 1024 for rows of
+// more than 2048 vectors), so fp32 results can differ from a row-resident
+// launch of another thread count in the last bits (the rounded residual is
+// identical, and a launch of the same thread layout is bit-identical).
+//
+// rms_chunk_kernel (plain): rows streamed in one or two 64 KB chunks that
+// stay in shared memory for both passes; see its comment below.
 //
 // Every wait is bounded: if a copy never completes, the CTA records
 // kStatusWaitTimeout in g_tma_status, waits (bounded) for its other copies,
