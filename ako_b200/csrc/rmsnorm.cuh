@@ -357,6 +357,20 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 1024, 2) \
     AKO_RMS_CASE(T, RES, 1, 1024, 4) \
     AKO_RMS_CASE(T, RES, 1, 1024, 8) \
+    AKO_RMS_CASE(T, RES, 1, 96, 2) \
+    AKO_RMS_CASE(T, RES, 1, 96, 4) \
+    AKO_RMS_CASE(T, RES, 1, 160, 2) \
+    AKO_RMS_CASE(T, RES, 1, 160, 4) \
+    AKO_RMS_CASE(T, RES, 1, 192, 2) \
+    AKO_RMS_CASE(T, RES, 1, 192, 4) \
+    AKO_RMS_CASE(T, RES, 1, 224, 2) \
+    AKO_RMS_CASE(T, RES, 1, 224, 4) \
+    AKO_RMS_CASE(T, RES, 1, 320, 2) \
+    AKO_RMS_CASE(T, RES, 1, 320, 4) \
+    AKO_RMS_CASE(T, RES, 1, 384, 2) \
+    AKO_RMS_CASE(T, RES, 1, 384, 4) \
+    AKO_RMS_CASE(T, RES, 1, 448, 2) \
+    AKO_RMS_CASE(T, RES, 1, 448, 4) \
     AKO_RMS_CASE(T, RES, 2, 64, 4) \
     AKO_RMS_CASE(T, RES, 2, 128, 1) \
     AKO_RMS_CASE(T, RES, 2, 128, 2) \

@@ -116,7 +116,8 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
     rng = np.random.default_rng(5)
     single = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
               (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
-              (1024, 1), (1024, 2), (1024, 4), (1024, 8)]
+              (1024, 1), (1024, 2), (1024, 4), (1024, 8), (96, 2), (96, 4), (160, 2), (160, 4), (192, 2), (192, 4),
+              (224, 2), (224, 4), (320, 2), (320, 4), (384, 2), (384, 4), (448, 2), (448, 4)]
     split = [(64, 4), (128, 2), (128, 4), (256, 2), (256, 4), (512, 2), (512, 4), (1024, 1), (1024, 2)]
     shapes = [(1, t, n) for t, n in single] + [(c, t, n) for c in (2, 4, 8) for t, n in split]
     try:
@@ -146,6 +147,27 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
                                   f"fp32 weight, shape {cl}x{tpr}x{nv}")
     finally:
         lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rmsnorm_fitted_thread_counts(cuda_device, dtype: str) -> None:
+    """Common widths that are not powers of two (2560 ... 13824) with enough
+    rows for the throughput table, which fits the thread count to the row
+    (e.g. 320 threads x 2 vectors for 5120 bf16 elements); plain and fused,
+    against the oracle, with ragged widths next to them."""
+    rng = np.random.default_rng(23)
+    for h in (2560, 3072, 3584, 5120, 6144, 7168, 12288, 13824, 5128, 12296):
+        rows = 600
+        x = normal(rng, (rows, h), 0, 1, dtype)
+        r = normal(rng, (rows, h), 0, 1, dtype)
+        w = normal(rng, (h,), 1, 0.1, dtype)
+        xt, rt, wt = (to_torch(a, dtype, cuda_device) for a in (x, r, w))
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
+        y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+        assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"fitted h={h}")
+        y1 = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
+        assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1), dtype, "rmsnorm", f"fitted h={h}")
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
