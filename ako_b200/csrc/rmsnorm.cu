@@ -38,8 +38,9 @@ constexpr int64_t kChunkedMinRowsBF16 = 1024;
 // SM): 0.92 against 0.75 of peak at 8192 x 32768 bf16, bit-identical output.
 // Below ~1024 rows (7 per SM) the persistent grid's start-up costs about
 // what it saves. The chunked kernel with one chunk per row (the row held in
-// shared memory instead of registers) measured level with this one. Other shapes keep the row-resident kernel, which measured equal or
-// faster (fp32, fused residual, 65536-wide rows).
+// shared memory instead of registers) measured level with this one. fp32
+// and fused rows keep the row-resident kernel, which measured equal or
+// faster staged.
 bool use_staged(const RmsArgs& a, int es, bool res) {
     if (g_mode == 1 || g_mode == 3) return false;
     if (g_mode == 2) return true;
