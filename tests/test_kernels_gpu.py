@@ -221,7 +221,7 @@ def test_staged_rmsnorm_matches_oracle(cuda_device, dtype: str) -> None:
 
 def _kernel_names(fn) -> str:
     """Names of the CUDA kernels ``fn`` launches, from torch's profiler."""
-    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA], acc_events=True) as prof:
         fn()
         torch.cuda.synchronize()
     return " ".join(e.name for e in prof.events())
@@ -286,6 +286,24 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
         y = kernels.rmsnorm_cuda_sm100(xv, w, 1e-6)
         assert_parity(C.rmsnorm(to_numpy(xv[:8]), to_numpy(w), 1e-6, dtype), to_numpy(y[:8]), dtype, "rmsnorm",
                       "wide strided")
+        # both persistent kernels captured in a CUDA graph replay the eager bytes
+        for rows, h in ((1024, 32768), (1024, 65536 // (es // 2) if es == 2 else 32768)):
+            xg, wg = rand((rows, h)), rand((h,), 1.0, 0.1)
+            mode = 0 if es == 2 else 2
+            assert lib.ako_b200_rmsnorm_set_staging(mode, 1 if mode == 2 else 0, 1 if mode == 2 else 0) == 0
+            eager = kernels.rmsnorm_cuda_sm100(xg, wg, 1e-6)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                kernels.rmsnorm_cuda_sm100(xg, wg, 1e-6)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                yg = kernels.rmsnorm_cuda_sm100(xg, wg, 1e-6)
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(yg, eager), (dtype, rows, h)
+            del graph
         torch.cuda.synchronize()
         assert _native.take_device_status() == 0
     finally:
