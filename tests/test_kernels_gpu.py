@@ -371,7 +371,7 @@ def test_rmsnorm_rejects_oversized_hidden_dim(cuda_device) -> None:
 
 
 # -------------------------------------------------------------------- rope
-ROPE_SHAPES = [(2, 6, 3, 8), (1, 1, 32, 128), (8, 1, 8, 128), (2, 128, 8, 64), (1, 64, 32, 128),
+ROPE_SHAPES = [(2, 6, 3, 8), (1, 1, 32, 128), (8, 1, 8, 128), (32, 1, 8, 128), (2, 128, 8, 64), (1, 64, 32, 128),
                (3, 17, 5, 128), (2, 9, 4, 256), (1, 5, 2, 6), (2, 4, 3, 2),
                # half head sizes that take 8-byte (36 pairs) and 4-byte (50, 10 pairs) accesses
                (2, 9, 3, 100), (1, 7, 4, 72), (2, 5, 6, 20)]
