@@ -229,6 +229,61 @@ rms_rows_kernel(const RmsArgs a) {
 
 constexpr int kGenericThreads = 256;
 
+// 16 bytes starting MIS bytes into the aligned 16-byte block p[0] (MIS even,
+// p[1] the next block): each output word joins two neighbouring words.
+template <int MIS>
+__device__ __forceinline__ uint4 shifted16(const uint4* p) {
+    if constexpr (MIS == 0) {
+        return *p;
+    } else {
+        const uint4 lo = p[0], hi = p[1];
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        constexpr int Q = MIS / 4, SH = (MIS % 4) * 8;
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = SH == 0 ? w[i + Q] : __funnelshift_r(w[i + Q], w[i + Q + 1], SH);
+        return make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Vector body of the generic kernel's output pass, for a weight of the row's
+// dtype at byte misalignment MIS (see rms_generic_kernel). A vector whose
+// aligned blocks reach outside the weight tensor (only the first or last
+// can, when the weight itself is not 16-byte aligned at its ends) reads its
+// weights element by element, so every access stays inside the tensor.
+template <typename T, bool RES, int MIS>
+__device__ __forceinline__ void generic_body_shifted(const RmsArgs& a, const T* xr, const T* ro, T* yr, int head,
+                                                     int nvec, float inv, const uint4* wv) {
+    constexpr int VEC = 16 / sizeof(T);
+    using P = Packed<T, VEC>;
+    const uintptr_t w_begin = reinterpret_cast<uintptr_t>(a.w);
+    const uintptr_t w_end = w_begin + static_cast<uintptr_t>(a.h) * sizeof(T);
+    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+        const int col = head + v * VEC;
+        const P xv = RES ? ld_cached<T, VEC>(ro + col) : ld_cached<T, VEC>(xr + col);
+        const uintptr_t blk = reinterpret_cast<uintptr_t>(wv + v);
+        P o;
+        if (blk >= w_begin && blk + (MIS == 0 ? 16 : 32) <= w_end) {
+            const uint4 wr = shifted16<MIS>(wv + v);
+            const P wp = *reinterpret_cast<const P*>(&wr);
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 f = get2<T, VEC>(xv, e);
+                const float2 w = get2<T, VEC>(wp, e);
+                put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), w.x), __fmul_rn(__fmul_rn(f.y, inv), w.y));
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 f = get2<T, VEC>(xv, e);
+                put2<T, VEC>(o, e, __fmul_rn(__fmul_rn(f.x, inv), load_weight(a.w, a.wdtype, col + e)),
+                             __fmul_rn(__fmul_rn(f.y, inv), load_weight(a.w, a.wdtype, col + e + 1)));
+            }
+        }
+        st_global<T, VEC>(yr + col, o);
+    }
+}
+
 template <typename T, bool RES>
 __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsArgs a) {
     constexpr int VEC = 16 / sizeof(T);
@@ -298,6 +353,25 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
     };
     for (int col = threadIdx.x; col < head; col += kGenericThreads) second_pass(col);
     for (int col = tail + threadIdx.x; col < a.h; col += kGenericThreads) second_pass(col);
+    // The body's weights: with the row's dtype they are 16 contiguous bytes
+    // per vector at a byte offset that is the same for every vector of the
+    // row, so they come from two aligned 16-byte loads and a shift chosen
+    // once per row; other weights are read element by element.
+    const uintptr_t wb = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(head) * sizeof(T);
+    if (a.wdtype == dtype_code<T>() && nvec > 0) {
+        const uint4* wv = reinterpret_cast<const uint4*>(wb & ~uintptr_t{15});
+        switch (static_cast<int>(wb & 15u)) {
+            case 0: generic_body_shifted<T, RES, 0>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 2: generic_body_shifted<T, RES, 2>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 4: generic_body_shifted<T, RES, 4>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 6: generic_body_shifted<T, RES, 6>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 8: generic_body_shifted<T, RES, 8>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 10: generic_body_shifted<T, RES, 10>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 12: generic_body_shifted<T, RES, 12>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            default: generic_body_shifted<T, RES, 14>(a, xr, ro, yr, head, nvec, inv, wv); break;
+        }
+        return;
+    }
     for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
         const int col = head + v * VEC;
         const P xv = RES ? ld_cached<T, VEC>(ro + col) : ld_cached<T, VEC>(xr + col);

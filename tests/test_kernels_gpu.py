@@ -100,6 +100,33 @@ def test_rmsnorm_strided_and_misaligned_rows(cuda_device, dtype: str) -> None:
         assert_parity(ref, to_numpy(y), dtype, "rmsnorm", "strided")
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rmsnorm_generic_weight_alignments(cuda_device, dtype: str) -> None:
+    """The any-width kernel reads a weight of the row's dtype through aligned
+    16-byte blocks shifted by the weight's misalignment within the row body:
+    every misalignment a weight view can have, ragged and aligned widths,
+    plain and fused, against the oracle (the first and last body vectors of a
+    view whose blocks would reach outside it read element by element)."""
+    rng = np.random.default_rng(41)
+    vec = 4 if dtype == O.F32 else 8
+    for h in (4100, 4096, 1000, 37):
+        rows = 6
+        x = normal(rng, (rows, h), 0, 1, dtype)
+        r = normal(rng, (rows, h), 0, 1, dtype)
+        wbase = normal(rng, (h + 2 * vec,), 1, 0.1, dtype)
+        xt, rt = to_torch(x, dtype, cuda_device), to_torch(r, dtype, cuda_device)
+        wt_base = to_torch(wbase, dtype, cuda_device)
+        for off in range(vec + 1):
+            w = wbase[off:off + h]
+            wt = wt_base[off:off + h]
+            y = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
+            assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y), dtype, "rmsnorm", f"h={h} weight offset {off}")
+            y, ro = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
+            y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+            np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+            assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"h={h} weight offset {off}")
+
+
 @pytest.mark.parametrize("dtype", (O.F16, O.BF16))
 def test_rmsnorm_fp32_weight(cuda_device, dtype: str) -> None:
     rng = np.random.default_rng(11)
