@@ -115,6 +115,23 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
         *out = rows <= 8 ? Shape{8, 256, 2} : Shape{4, 512, 2};
         return true;
     }
+    // Narrow rows in bulk: a warp per row (four rows per 128-thread CTA)
+    // with 4 or 8 vectors a thread beats a 64-thread CTA per row, whose tiny
+    // CTAs cost more to schedule than their rows take to stream. Measured on
+    // B200 (bf16, fp16, fp32; 1024-65536 rows): plain rows of 65-128 vectors
+    // 0.40-0.55 -> 0.78-0.99 of peak at 65536 rows and better from 4096 rows
+    // on; fused rows of 65-112 vectors 0.79-0.93 -> 0.97-0.99 at 65536 rows,
+    // better from 16384 (mixed below 8192; 128-vector rows level); plain rows
+    // of 129-224 vectors 0.68-0.82 -> 0.74-0.99 at 65536 rows, better from
+    // 16384.
+    if (nvec > 64 && nvec <= 128 && (!residual || rows >= 8192)) {
+        *out = Shape{1, 32, 4};
+        return true;
+    }
+    if (!residual && nvec > 128 && nvec <= 224 && rows >= 16384) {
+        *out = Shape{1, 32, 8};
+        return true;
+    }
     static const Shape fused[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 128, 2},
                                   {1, 256, 2}, {1, 512, 2}, {1, 512, 4}, {1, 1024, 4}};
     static const Shape plain[] = {{1, 32, 1},  {1, 32, 2},  {1, 64, 2},  {1, 64, 4},

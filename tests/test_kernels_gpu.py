@@ -101,6 +101,30 @@ def test_rmsnorm_strided_and_misaligned_rows(cuda_device, dtype: str) -> None:
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+def test_rmsnorm_narrow_rows_in_bulk(cuda_device, dtype: str) -> None:
+    """Narrow rows in many rows take a warp per row with 4 or 8 vectors a
+    thread (65-224 vectors, from 8192 or 16384 rows): plain and fused against
+    the oracle on a sample of rows, including partial last CTAs."""
+    vec = 4 if dtype == O.F32 else 8
+    g = torch.Generator(device=cuda_device).manual_seed(29)
+    tdt = TORCH_DTYPE[dtype]
+    for nvec in (65, 96, 128, 160, 224):
+        h = nvec * vec
+        rows = 16387
+        x = torch.randn(rows, h, generator=g, device=cuda_device).to(tdt)
+        r = torch.randn(rows, h, generator=g, device=cuda_device).to(tdt)
+        w = (torch.randn(h, generator=g, device=cuda_device) * 0.1 + 1).to(tdt)
+        sel = list(range(0, rows, 1021)) + [rows - 3, rows - 2, rows - 1]
+        y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+        assert_parity(C.rmsnorm(to_numpy(x[sel]), to_numpy(w), 1e-6, dtype), to_numpy(y[sel]), dtype, "rmsnorm",
+                      f"narrow h={h}")
+        y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+        y_ref, ro_ref = C.rmsnorm_residual(to_numpy(x[sel]), to_numpy(r[sel]), to_numpy(w), 1e-5, dtype)
+        np.testing.assert_array_equal(to_numpy(ro[sel]), ro_ref)
+        assert_parity(y_ref, to_numpy(y[sel]), dtype, "rmsnorm_residual", f"narrow h={h}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 def test_rmsnorm_generic_weight_alignments(cuda_device, dtype: str) -> None:
     """The any-width kernel reads a weight of the row's dtype through aligned
     16-byte blocks shifted by the weight's misalignment within the row body:
