@@ -78,16 +78,17 @@ bool use_chunked(const RmsArgs& a, int dtype) {
 //    loads come from several SMs at once.
 // Rows whose vector count is not a power of two (5120 bf16 elements are 640
 // vectors) leave up to half of a power-of-two CTA idle. With the table's
-// vectors per thread, take the multiple of 32 threads that just covers the
-// row when that thread count is built (96-448). 5120-wide bf16 rows at 8192
+// vectors per thread, take the smallest built thread count (multiples of 32
+// from 96 to 896) that covers the row, when it is below the table's power of
+// two. 5120-wide bf16 rows at 8192
 // rows went from 0.86 to 0.94 of peak (fused) and from 0.69 to 0.82 (plain),
 // at 32768 rows from 0.98 to 1.07 and from 0.85 to 1.02 (B200, cold L2).
 Shape fit_threads(Shape s, int64_t nvec) {
-    static const int kFitted[] = {96, 160, 192, 224, 320, 384, 448};
+    static const int kFitted[] = {96, 160, 192, 224, 320, 384, 448, 640, 768, 896};
     if (s.cluster != 1 || s.tpr < 128 || (s.nv != 2 && s.nv != 4)) return s;
-    const int64_t need = ((nvec + s.nv - 1) / s.nv + 31) / 32 * 32;
+    const int64_t need = (nvec + s.nv - 1) / s.nv;
     for (int t : kFitted)
-        if (t == need && t < s.tpr) return Shape{1, t, s.nv};
+        if (t >= need) return t < s.tpr ? Shape{1, t, s.nv} : s;
     return s;
 }
 
@@ -289,7 +290,8 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
                                     {128, 16}, {256, 1},  {256, 2},  {256, 4},  {256, 8},  {512, 1}, {512, 2},
                                     {512, 4},  {512, 8},  {1024, 1}, {1024, 2}, {1024, 4}, {1024, 8}, {96, 2},
                                     {96, 4},   {160, 2},  {160, 4},  {192, 2},  {192, 4},  {224, 2}, {224, 4},
-                                    {320, 2},  {320, 4},  {384, 2},  {384, 4},  {448, 2},  {448, 4}};
+                                    {320, 2},  {320, 4},  {384, 2},  {384, 4},  {448, 2},  {448, 4}, {640, 2},
+                                    {640, 4},  {768, 2},  {768, 4},  {896, 2},  {896, 4}};
     static const int split[][2] = {{64, 4},  {128, 1}, {128, 2}, {128, 4}, {256, 1}, {256, 2},
                                    {256, 4}, {512, 1}, {512, 2}, {512, 4}, {1024, 1}, {1024, 2}};
     bool ok = false;

@@ -445,6 +445,12 @@ int launch_rows_kernel(Kernel kernel, int64_t grid, int threads, int cluster, co
     AKO_RMS_CASE(T, RES, 1, 384, 4) \
     AKO_RMS_CASE(T, RES, 1, 448, 2) \
     AKO_RMS_CASE(T, RES, 1, 448, 4) \
+    AKO_RMS_CASE(T, RES, 1, 640, 2) \
+    AKO_RMS_CASE(T, RES, 1, 640, 4) \
+    AKO_RMS_CASE(T, RES, 1, 768, 2) \
+    AKO_RMS_CASE(T, RES, 1, 768, 4) \
+    AKO_RMS_CASE(T, RES, 1, 896, 2) \
+    AKO_RMS_CASE(T, RES, 1, 896, 4) \
     AKO_RMS_CASE(T, RES, 2, 64, 4) \
     AKO_RMS_CASE(T, RES, 2, 128, 1) \
     AKO_RMS_CASE(T, RES, 2, 128, 2) \

@@ -168,7 +168,8 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
     single = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
               (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
               (1024, 1), (1024, 2), (1024, 4), (1024, 8), (96, 2), (96, 4), (160, 2), (160, 4), (192, 2), (192, 4),
-              (224, 2), (224, 4), (320, 2), (320, 4), (384, 2), (384, 4), (448, 2), (448, 4)]
+              (224, 2), (224, 4), (320, 2), (320, 4), (384, 2), (384, 4), (448, 2), (448, 4), (640, 2), (640, 4),
+              (768, 2), (768, 4), (896, 2), (896, 4)]
     split = [(64, 4), (128, 2), (128, 4), (256, 2), (256, 4), (512, 2), (512, 4), (1024, 1), (1024, 2)]
     shapes = [(1, t, n) for t, n in single] + [(c, t, n) for c in (2, 4, 8) for t, n in split]
     try:
@@ -207,7 +208,7 @@ def test_rmsnorm_fitted_thread_counts(cuda_device, dtype: str) -> None:
     (e.g. 320 threads x 2 vectors for 5120 bf16 elements); plain and fused,
     against the oracle, with ragged widths next to them."""
     rng = np.random.default_rng(23)
-    for h in (2560, 3072, 3584, 5120, 6144, 7168, 12288, 13824, 5128, 12296):
+    for h in (2560, 3072, 3584, 5120, 6144, 7168, 12288, 13824, 5128, 12296, 4608, 9216, 11264):
         rows = 600
         x = normal(rng, (rows, h), 0, 1, dtype)
         r = normal(rng, (rows, h), 0, 1, dtype)
