@@ -38,9 +38,9 @@ def cuda_device():
 
 
 def reference_path() -> Path | None:
-    """Source tree of the reference (``AKO_REFERENCE``, else the build
-    container's read-only copy), when this machine has one; GPU boxes have
-    none, and only CPU tests use it."""
-    cand = os.environ.get("AKO_REFERENCE", "/root/reference")
-    p = Path(cand)
+    """Directory holding the reference's ``ako`` package (``AKO_REFERENCE``,
+    else the offline install under ``baseline/_ref``), when there is one;
+    only CPU tests use it."""
+    cand = os.environ.get("AKO_REFERENCE")
+    p = Path(cand) if cand else Path(__file__).resolve().parents[1] / "baseline" / "_ref"
     return p if (p / "ako" / "__init__.py").exists() else None
