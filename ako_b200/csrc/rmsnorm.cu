@@ -163,6 +163,33 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
     return false;
 }
 
+// The kernel run() picks for a call, without launching it: kernel 0
+// row-resident (cluster x threads x vectors), 1 staged and 2 chunked
+// (threads x vectors, cluster 1), 3 any-width.
+struct Plan {
+    int kernel, cluster, threads, vectors;
+};
+
+Plan plan_for(const RmsArgs& a, int dtype, bool res, bool vector_ok) {
+    const int es = dtype_size(dtype);
+    if (vector_ok && !res && use_chunked(a, dtype)) {
+        const int chunks = rms_chunks_for(a.h, es);
+        if (chunks > 0) return Plan{2, 1, 1024, 4 * chunks};
+    }
+    if (vector_ok && use_staged(a, es, res)) {
+        const bool chosen = g_mode == 0;
+        const int stages = g_stages > 0 ? g_stages : chosen ? 1 : 4;
+        const int ctas = g_ctas_per_sm > 0 ? g_ctas_per_sm : chosen ? 1 : 2;
+        int threads = 0, nv = 0;
+        if (rms_staged_shape(a.h, es, res, stages, ctas, &threads, &nv)) return Plan{1, 1, threads, nv};
+    }
+    if (vector_ok) {
+        Shape s;
+        if (pick_shape(a.h / (16 / es), a.rows, res, es, &s)) return Plan{0, s.cluster, s.tpr, s.nv};
+    }
+    return Plan{3, 1, 256, 0};
+}
+
 template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok && !RES && use_chunked(a, dtype_code<T>())) {
@@ -304,6 +331,25 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm launch shape (cluster %d, %d threads, %d vectors) is not built",
                          cluster, threads_per_row, vectors_per_thread);
     g_override = {cluster, threads_per_row, vectors_per_thread};
+    return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_rmsnorm_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int residual, int aligned,
+                                     int* kernel, int* cluster, int* threads_per_row, int* vectors_per_thread) {
+    clear_error();
+    if (kernel == nullptr || cluster == nullptr || threads_per_row == nullptr || vectors_per_thread == nullptr)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_rmsnorm_plan: null output pointer");
+    const int rc = check_common("ako_b200_rmsnorm_plan", n_rows, hidden_dim, dtype, dtype);
+    if (rc != AKO_B200_OK) return rc;
+    RmsArgs a{};
+    a.rows = n_rows;
+    a.h = static_cast<int>(hidden_dim);
+    const bool vector_ok = aligned != 0 && (hidden_dim * dtype_size(dtype)) % 16 == 0;
+    const Plan pl = plan_for(a, dtype, residual != 0, vector_ok);
+    *kernel = pl.kernel;
+    *cluster = pl.cluster;
+    *threads_per_row = pl.threads;
+    *vectors_per_thread = pl.vectors;
     return AKO_B200_OK;
 }
 

@@ -508,9 +508,15 @@ int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
 // (rmsnorm_tma.cu); -1 when the row is too wide for it.
 int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st);
 
-// Plain rows of 4097-8192 vectors streamed in two shared-memory chunks per
-// row (rmsnorm_tma.cu); -1 for other rows.
+// Plain rows of 2049-8192 vectors streamed through shared memory in one or
+// two chunks per row (rmsnorm_tma.cu); -1 for other rows.
 int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st);
+
+// Host-side shapes of the two persistent kernels (no launch): the staged
+// kernel's threads and vectors per thread (false when it does not take the
+// row), and the chunked kernel's chunks per row (0 when it does not).
+bool rms_staged_shape(int h, int es, bool res, int stages, int ctas_per_sm, int* threads_out, int* nv_out);
+int rms_chunks_for(int h, int es);
 
 // Reads and clears the staged kernels' device status word (synchronizing).
 int take_staged_status(int* status);

@@ -426,17 +426,24 @@ int launch_dtype(const RmsArgs& a, int threads, int nv, int stages, int ctas_per
 
 // Staged launch for rows of `h` 16-bit or fp32 elements (16-byte aligned rows,
 // h * sizeof(T) a multiple of 16); -1 when the row is too wide for it.
-int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st) {
-    const int es = dtype_size(dtype);
-    const int nvec = a.h * es / 16;
+bool rms_staged_shape(int h, int es, bool res, int stages, int ctas_per_sm, int* threads_out, int* nv_out) {
+    const int nvec = h * es / 16;
     // 256 threads up to 8 vectors each; wider rows take 1024 threads of 4 or 8.
     int threads = kTmaThreads;
     if (nvec > 8 * kTmaThreads) threads = kTmaWideThreads;
     int nv = threads == kTmaThreads ? 1 : 4;
     while (nv * threads < nvec) nv *= 2;
-    if (nv > 8 || stages < 1 || stages > kMaxStages || ctas_per_sm < 1) return -1;
-    const int row_bytes = a.h * es;
-    if (static_cast<int64_t>(stages) * (res ? 2 : 1) * row_bytes > 200 * 1024) return -1;
+    if (nv > 8 || stages < 1 || stages > kMaxStages || ctas_per_sm < 1) return false;
+    const int row_bytes = h * es;
+    if (static_cast<int64_t>(stages) * (res ? 2 : 1) * row_bytes > 200 * 1024) return false;
+    *threads_out = threads;
+    *nv_out = nv;
+    return true;
+}
+
+int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st) {
+    int threads = 0, nv = 0;
+    if (!rms_staged_shape(a.h, dtype_size(dtype), res, stages, ctas_per_sm, &threads, &nv)) return -1;
     switch (dtype) {
         case AKO_B200_F32: return res ? launch_dtype<float, true>(a, threads, nv, stages, ctas_per_sm, st)
                                       : launch_dtype<float, false>(a, threads, nv, stages, ctas_per_sm, st);
@@ -449,12 +456,17 @@ int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int cta
 
 // Chunked launch for plain rows of 2049-8192 16-byte vectors (16-byte aligned
 // rows): one chunk per row up to 4096 vectors, two above; -1 for other rows.
-int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st) {
-    const int es = dtype_size(dtype);
-    const int64_t nvec = static_cast<int64_t>(a.h) * es / 16;
+int rms_chunks_for(int h, int es) {
+    const int64_t nvec = static_cast<int64_t>(h) * es / 16;
     const int64_t per_chunk = static_cast<int64_t>(kTmaWideThreads) * kChunkNV;
-    if (nvec <= per_chunk / 2 || nvec > 2 * per_chunk) return -1;
-    const bool two = nvec > per_chunk;
+    if (nvec <= per_chunk / 2 || nvec > 2 * per_chunk) return 0;
+    return nvec > per_chunk ? 2 : 1;
+}
+
+int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st) {
+    const int chunks = rms_chunks_for(a.h, dtype_size(dtype));
+    if (chunks == 0) return -1;
+    const bool two = chunks == 2;
     switch (dtype) {
         case AKO_B200_F32: return two ? launch_chunked<float, 2>(a, st) : launch_chunked<float, 1>(a, st);
         case AKO_B200_F16: return two ? launch_chunked<__half, 2>(a, st) : launch_chunked<__half, 1>(a, st);

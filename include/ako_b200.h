@@ -186,6 +186,21 @@ int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_pe
 int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm);
 
 /*
+ * The kernel an RMSNorm call of `n_rows` x `hidden_dim` in `dtype` would run,
+ * without launching anything (host only; no GPU needed): *kernel is 0 for the
+ * row-resident kernel (a thread-block cluster of *cluster CTAs, each row
+ * slice held by *threads_per_row threads with *vectors_per_thread 16-byte
+ * vectors), 1 for the staged and 2 for the chunked persistent kernel
+ * (threads and vectors per thread; cluster 1), 3 for the any-width kernel.
+ * `residual` selects the fused form; `aligned` says whether the call's
+ * pointers and row strides are 16-byte aligned. Follows the built-in choice
+ * and any measurement override in force. Not part of the reference's
+ * interface; it has no counterpart there.
+ */
+int ako_b200_rmsnorm_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int residual, int aligned,
+                          int* kernel, int* cluster, int* threads_per_row, int* vectors_per_thread);
+
+/*
  * Reads and clears the device status word of this library's kernels on the
  * current device: 0, or 1 when a kernel's bounded wait for an asynchronous
  * copy ran out (the kernel then left its rows unwritten). Synchronizes the

@@ -1,0 +1,106 @@
+"""Host-side launch choices of the RMSNorm entry points (no GPU needed).
+
+``ako_b200_rmsnorm_plan`` reports the kernel and launch shape a call would
+get from the built-in choice, through the same code path the launch takes.
+These cases pin the measured rules: the tables for the benchmark's widths,
+fitted thread counts for widths that are not a power of two of 16-byte
+vectors, a warp per row for narrow rows in bulk, clusters for decode and for
+65536-wide fused rows, the staged and chunked persistent kernels for wide
+plain 16-bit rows, and the any-width kernel for unaligned calls.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from ako_b200 import _native
+
+F32, F16, BF16 = 0, 1, 2
+ROWS, STAGED, CHUNKED, GENERIC = 0, 1, 2, 3
+
+
+def plan(rows: int, h: int, dtype: int, residual: bool, aligned: bool = True) -> tuple[int, int, int, int]:
+    out = [ctypes.c_int() for _ in range(4)]
+    rc = _native.lib().ako_b200_rmsnorm_plan(rows, h, dtype, int(residual), int(aligned), *(ctypes.byref(o) for o in out))
+    assert rc == 0, _native.lib().ako_b200_last_error()
+    return tuple(o.value for o in out)
+
+
+@pytest.fixture(autouse=True)
+def _built_in_choice():
+    lib = _native.lib()
+    lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
+    lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+    yield
+    lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
+    lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+
+
+@pytest.mark.parametrize(
+    "rows, h, dtype, residual, expected",
+    [
+        # the benchmark: the headline cell, config 1, config 2 widths
+        (32768, 16384, BF16, True, (ROWS, 1, 512, 4)),
+        (2048, 4096, F32, False, (ROWS, 1, 256, 4)),
+        (8192, 2048, BF16, True, (ROWS, 1, 128, 2)),
+        (8192, 4096, F16, True, (ROWS, 1, 256, 2)),
+        (8192, 8192, BF16, True, (ROWS, 1, 512, 2)),
+        # decode: latency shapes and clusters
+        (1, 4096, BF16, True, (ROWS, 1, 512, 1)),
+        (1, 16384, BF16, True, (ROWS, 4, 512, 1)),
+        (64, 16384, BF16, True, (ROWS, 4, 256, 2)),
+        # fitted thread counts (5120 bf16 = 640 vectors, 4608 = 576)
+        (8192, 5120, BF16, True, (ROWS, 1, 320, 2)),
+        (8192, 5120, BF16, False, (ROWS, 1, 160, 4)),
+        (8192, 4608, BF16, True, (ROWS, 1, 320, 2)),
+        (8192, 9216, BF16, False, (ROWS, 1, 320, 4)),
+        (8192, 2304, F32, True, (ROWS, 1, 320, 2)),
+        # narrow rows in bulk: a warp per row
+        (32768, 1024, BF16, False, (ROWS, 1, 32, 4)),
+        (4096, 1024, BF16, True, (ROWS, 1, 64, 2)),
+        (16384, 1024, BF16, True, (ROWS, 1, 32, 4)),
+        (16384, 1536, BF16, False, (ROWS, 1, 32, 8)),
+        (8192, 1536, BF16, False, (ROWS, 1, 64, 4)),
+        # wide rows: staged (16385-32768 16-bit elements) and chunked (32769-65536)
+        (8192, 32768, BF16, False, (STAGED, 1, 1024, 4)),
+        (512, 32768, BF16, False, (ROWS, 1, 1024, 4)),
+        (8192, 32768, BF16, True, (ROWS, 1, 1024, 4)),
+        (512, 65536, F16, False, (CHUNKED, 1, 1024, 8)),
+        (512, 65536, BF16, False, (ROWS, 1, 1024, 8)),
+        (2048, 65536, BF16, False, (CHUNKED, 1, 1024, 8)),
+        (2048, 40960, BF16, False, (CHUNKED, 1, 1024, 8)),
+        (8192, 32768, F32, False, (ROWS, 1, 1024, 8)),
+        (4096, 65536, BF16, True, (ROWS, 8, 256, 4)),
+    ],
+)
+def test_built_in_choice(rows, h, dtype, residual, expected) -> None:
+    assert plan(rows, h, dtype, residual) == expected
+
+
+def test_unaligned_and_ragged_calls_take_the_any_width_kernel() -> None:
+    assert plan(8192, 4096, BF16, True, aligned=False)[0] == GENERIC
+    assert plan(8192, 4100, BF16, False)[0] == GENERIC
+    assert plan(8192, 4100, F32, False)[0] == ROWS  # 16400-byte fp32 rows are whole vectors
+
+
+def test_measurement_overrides_are_followed() -> None:
+    lib = _native.lib()
+    assert lib.ako_b200_rmsnorm_set_launch(2, 512, 4) == 0
+    assert plan(8192, 8192, BF16, True) == (ROWS, 2, 512, 4)
+    assert lib.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
+    assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
+    assert plan(8192, 4096, BF16, True) == (STAGED, 1, 256, 2)
+    assert lib.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
+    assert plan(8192, 32768, BF16, False) == (ROWS, 1, 1024, 4)
+    assert lib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
+    assert plan(8192, 24576, BF16, False) == (CHUNKED, 1, 1024, 4)
+
+
+def test_invalid_arguments_are_rejected() -> None:
+    out = [ctypes.c_int() for _ in range(4)]
+    lib = _native.lib()
+    assert lib.ako_b200_rmsnorm_plan(8, 4096, 7, 0, 1, *(ctypes.byref(o) for o in out)) == 2
+    assert lib.ako_b200_rmsnorm_plan(8, 0, BF16, 0, 1, *(ctypes.byref(o) for o in out)) == 1
+    assert lib.ako_b200_rmsnorm_plan(8, 4096, BF16, 0, 1, None, None, None, None) == 1
