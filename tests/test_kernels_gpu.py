@@ -279,6 +279,38 @@ def _kernel_names(fn) -> str:
     return " ".join(e.name for e in prof.events())
 
 
+def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
+    """``ako_b200_rmsnorm_plan`` (host only) names the kernel and launch shape
+    that the call then runs: the profiler's kernel name carries the same
+    kernel and, for the row-resident kernel, the same template shape."""
+    import ctypes
+    import re
+
+    lib = _native.lib()
+    names = {0: "rms_rows_kernel", 1: "rms_tma_kernel", 2: "rms_chunk_kernel", 3: "rms_generic_kernel"}
+    codes = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+    cases = [(32768, 16384, torch.bfloat16, True), (2048, 4096, torch.float32, False), (8192, 5120, torch.bfloat16, True),
+             (8192, 5120, torch.float16, False), (32768, 1024, torch.bfloat16, False), (1, 16384, torch.bfloat16, True),
+             (8192, 32768, torch.bfloat16, False), (2048, 65536, torch.float16, False), (4096, 65536, torch.bfloat16, True),
+             (8192, 4100, torch.bfloat16, False), (16384, 1536, torch.float32, False)]
+    for rows, h, dt, residual in cases:
+        out = [ctypes.c_int() for _ in range(4)]
+        assert lib.ako_b200_rmsnorm_plan(rows, h, codes[dt], int(residual), 1, *(ctypes.byref(o) for o in out)) == 0
+        kernel, cluster, tpr, nv = (o.value for o in out)
+        x = torch.randn(rows, h, device=cuda_device).to(dt)
+        w = torch.ones(h, device=cuda_device, dtype=dt)
+        if residual:
+            got = _kernel_names(lambda: kernels.rmsnorm_residual_cuda_sm100(x, x, w, 1e-5))
+        else:
+            got = _kernel_names(lambda: kernels.rmsnorm_cuda_sm100(x, w, 1e-6))
+        assert names[kernel] in got, (rows, h, dt, residual, kernel, got[:200])
+        if kernel == 0:
+            m = re.search(r"rms_rows_kernel<[^,]+, (\d+), (\d+), (?:true|false|1|0), (\d+)>", got)
+            assert m is not None, got[:300]
+            assert (int(m.group(3)), int(m.group(1)), int(m.group(2))) == (cluster, tpr, nv), (rows, h, got[:300])
+        del x
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
     """Rows of 2049-8192 vectors through the 1024-thread staged kernel (the
