@@ -174,3 +174,23 @@ def test_staging_hook_validation(lib) -> None:
     assert lib.ako_b200_rmsnorm_set_staging(4, 0, 0) == 1
     assert lib.ako_b200_rmsnorm_set_staging(2, 9, 1) == 1
     assert lib.ako_b200_take_device_status(None) == 1
+
+
+def test_host_pipeline_chunking_and_argument_checks() -> None:
+    """The host-buffer pipeline's chunk arithmetic (one launch per chunk of
+    32 MB per operand) and its argument errors, all decided before any GPU
+    work."""
+    from ako_b200 import host
+
+    assert host.DEFAULT_CHUNK_BYTES == 32 << 20
+    assert host.launches_per_call(32768, 16384, 2) == 32  # 1024 rows of 32 KB per chunk
+    assert host.launches_per_call(1000, 16384, 2) == 1
+    assert host.launches_per_call(1025, 16384, 2, chunk_rows=1024) == 2
+    assert host.launches_per_call(0, 4096, 2) == 0
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="Shape mismatch"):
+        host.rmsnorm_residual_host(x, torch.zeros(4, 9, dtype=torch.bfloat16), torch.ones(8))
+    with pytest.raises(ValueError, match="supports float32/float16/bfloat16"):
+        host.rmsnorm_residual_host(x.to(torch.int32), x.to(torch.int32), torch.ones(8))
+    with pytest.raises(ValueError, match="weight must live on the target CUDA device"):
+        host.rmsnorm_residual_host(x, x, torch.ones(8))
