@@ -156,19 +156,43 @@ int launch(SwigluArgs a, bool flat, cudaStream_t st) {
     return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
 }
 
+// Launch choice for a call: bytes per access (16, 4 for decode-sized
+// problems, or the element size when the operands are not 16-byte aligned),
+// CTA size and vectors per thread.
+struct SwigluPlan {
+    int access_bytes, threads, unroll;
+};
+
+SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat) {
+    if (vector_ok && g_threads == 0 && rows * h <= kTinyElements) {
+        // Decode-sized problems are latency-bound: two elements per thread
+        // (4-byte accesses) spread them over four times the threads, which
+        // shortens each thread's chain of conversions, exponentials and
+        // reciprocals. In CUDA graphs on B200 this is 0.1 us faster per call
+        // for fp16 and fp32 rows of 5632-14336 at 1-2 rows and the same for
+        // bf16; above 2^15 elements 16-byte accesses are as fast or faster.
+        return SwigluPlan{4, 128, 1};
+    }
+    if (vector_ok) {
+        // 256-thread CTAs with one vector of each input per thread (32
+        // registers, a full SM of threads) are within 1% of the best shape on
+        // every cell measured on B200 (F 5632..14336, 2048..16384 rows, bf16
+        // and fp16) and up to 10% faster than two vectors per thread, except
+        // dense operands of 2^24 vectors and more, which stream 2-4% faster
+        // with two. Small problems (decode rows) use 128-thread CTAs, so the
+        // few vectors spread over many SMs (measured fastest up to ~64 rows of
+        // 5632..14336).
+        const int64_t total = rows * (h * es / 16);
+        const bool small = total < static_cast<int64_t>(sm_count()) * kThreads * 4;
+        const bool huge_dense = flat && total >= (int64_t{1} << 24);
+        return SwigluPlan{16, g_threads > 0 ? g_threads : (small ? 128 : kThreads),
+                          g_unroll > 0 ? g_unroll : (huge_dense ? 2 : 1)};
+    }
+    return SwigluPlan{es, 256, 4};
+}
+
 template <typename T, int VEC>
-int launch_vec(const SwigluArgs& a, bool flat, cudaStream_t st) {
-    // 256-thread CTAs with one vector of each input per thread (32 registers,
-    // a full SM of threads) are within 1% of the best shape on every cell
-    // measured on B200 (F 5632..14336, 2048..16384 rows, bf16 and fp16) and
-    // up to 10% faster than two vectors per thread, except dense operands of
-    // 2^24 vectors and more, which stream 2-4% faster with two. Small problems
-    // (decode rows) use 128-thread CTAs, so the few vectors spread over many
-    // SMs (measured fastest up to ~64 rows of 5632..14336).
-    const bool small = a.total < static_cast<int64_t>(sm_count()) * kThreads * 4;
-    const bool huge_dense = flat && a.total >= (int64_t{1} << 24);
-    const int threads = g_threads > 0 ? g_threads : (small ? 128 : kThreads);
-    const int unroll = g_unroll > 0 ? g_unroll : (huge_dense ? 2 : 1);
+int launch_vec(const SwigluArgs& a, bool flat, int threads, int unroll, cudaStream_t st) {
     switch (threads * 16 + unroll) {
         case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, st);
         case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, st);
@@ -183,26 +207,13 @@ int launch_vec(const SwigluArgs& a, bool flat, cudaStream_t st) {
 template <typename T>
 int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaStream_t st) {
     constexpr int VEC = 16 / sizeof(T);
-    if (vector_ok && g_threads == 0 && rows * h <= kTinyElements) {
-        // Decode-sized problems are latency-bound: two elements per thread
-        // (4-byte accesses) spread them over four times the threads, which
-        // shortens each thread's chain of conversions, exponentials and
-        // reciprocals. In CUDA graphs on B200 this is 0.1 us faster per call
-        // for fp16 and fp32 rows of 5632-14336 at 1-2 rows and the same for
-        // bf16; above 2^15 elements 16-byte accesses are as fast or faster.
-        constexpr int V2 = 4 / static_cast<int>(sizeof(T));
-        a.per_row = h / V2;
-        a.total = rows * a.per_row;
-        return launch<T, V2, 1, 128>(a, flat, st);
-    }
-    if (vector_ok) {
-        a.per_row = h / VEC;
-        a.total = rows * a.per_row;
-        return launch_vec<T, VEC>(a, flat, st);
-    }
-    a.per_row = h;
-    a.total = rows * h;
-    return launch<T, 1, 4, 256>(a, flat, st);
+    const SwigluPlan p = swiglu_plan(rows, h, static_cast<int>(sizeof(T)), vector_ok, flat);
+    const int per_access = p.access_bytes / static_cast<int>(sizeof(T));
+    a.per_row = h / per_access;
+    a.total = rows * a.per_row;
+    if (!vector_ok) return launch<T, 1, 4, 256>(a, flat, st);
+    if (p.access_bytes == 4) return launch<T, 4 / sizeof(T), 1, 128>(a, flat, st);
+    return launch_vec<T, VEC>(a, flat, p.threads, p.unroll, st);
 }
 
 }  // namespace
@@ -238,6 +249,23 @@ extern "C" int ako_b200_swiglu(const void* gate, int64_t gate_row_stride, const 
         case AKO_B200_F16: return run<__half>(a, n_rows, hidden_dim, vector_ok, flat, st);
         default: return run<__nv_bfloat16>(a, n_rows, hidden_dim, vector_ok, flat, st);
     }
+}
+
+extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int aligned, int dense,
+                                    int* access_bytes, int* threads, int* vectors_per_thread) {
+    clear_error();
+    if (access_bytes == nullptr || threads == nullptr || vectors_per_thread == nullptr)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_swiglu_plan: null output pointer");
+    const int es = dtype_size(dtype);
+    if (es == 0) return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "ako_b200_swiglu_plan: unsupported dtype code %d", dtype);
+    if (n_rows < 1 || hidden_dim < 1)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_swiglu_plan: empty problem");
+    const bool vector_ok = aligned != 0 && (hidden_dim * es) % 16 == 0;
+    const SwigluPlan p = swiglu_plan(n_rows, hidden_dim, es, vector_ok, dense != 0);
+    *access_bytes = p.access_bytes;
+    *threads = p.threads;
+    *vectors_per_thread = p.unroll;
+    return AKO_B200_OK;
 }
 
 extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {

@@ -227,6 +227,19 @@ int ako_b200_rope_set_launch(int heads_per_thread);
 int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
 
 /*
+ * The launch a SwiGLU call of `n_rows` x `hidden_dim` in `dtype` would get,
+ * without launching anything (host only; no GPU needed): bytes per access
+ * (16; 4 for decode-sized problems; the element size when the operands are
+ * not 16-byte aligned), threads per CTA and vectors per thread. `aligned`
+ * says whether the call's pointers and row strides are 16-byte aligned,
+ * `dense` whether all three operands are contiguous. Follows the built-in
+ * choice and any measurement override in force. Not part of the reference's
+ * interface; it has no counterpart there.
+ */
+int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int aligned, int dense,
+                         int* access_bytes, int* threads, int* vectors_per_thread);
+
+/*
  * Programmatic dependent launch: with `enable` = 1 (the default) every
  * kernel of this library is launched with programmatic stream serialization,
  * so it may start while the previous kernel in the stream drains; it waits

@@ -1,12 +1,15 @@
-"""Host-side launch choices of the RMSNorm entry points (no GPU needed).
+"""Host-side launch choices of the RMSNorm and SwiGLU entry points (no GPU
+needed).
 
-``ako_b200_rmsnorm_plan`` reports the kernel and launch shape a call would
-get from the built-in choice, through the same code path the launch takes.
-These cases pin the measured rules: the tables for the benchmark's widths,
-fitted thread counts for widths that are not a power of two of 16-byte
-vectors, a warp per row for narrow rows in bulk, clusters for decode and for
-65536-wide fused rows, the staged and chunked persistent kernels for wide
-plain 16-bit rows, and the any-width kernel for unaligned calls.
+``ako_b200_rmsnorm_plan`` and ``ako_b200_swiglu_plan`` report the kernel and
+launch shape a call would get from the built-in choice, through the same code
+the launch takes. These cases pin the measured rules: for RMSNorm the tables
+for the benchmark's widths, fitted thread counts for widths that are not a
+power of two of 16-byte vectors, a warp per row for narrow rows in bulk,
+clusters for decode and for 65536-wide fused rows, the staged and chunked
+persistent kernels for wide plain 16-bit rows, and the any-width kernel for
+unaligned calls; for SwiGLU the access width, CTA size and vectors per thread
+by problem size and layout.
 """
 
 from __future__ import annotations
@@ -104,3 +107,39 @@ def test_invalid_arguments_are_rejected() -> None:
     assert lib.ako_b200_rmsnorm_plan(8, 4096, 7, 0, 1, *(ctypes.byref(o) for o in out)) == 2
     assert lib.ako_b200_rmsnorm_plan(8, 0, BF16, 0, 1, *(ctypes.byref(o) for o in out)) == 1
     assert lib.ako_b200_rmsnorm_plan(8, 4096, BF16, 0, 1, None, None, None, None) == 1
+
+
+def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool = True) -> tuple[int, int, int]:
+    out = [ctypes.c_int() for _ in range(3)]
+    rc = _native.lib().ako_b200_swiglu_plan(rows, f, dtype, int(aligned), int(dense), *(ctypes.byref(o) for o in out))
+    assert rc == 0, _native.lib().ako_b200_last_error()
+    return tuple(o.value for o in out)
+
+
+@pytest.mark.parametrize(
+    "rows, f, dtype, aligned, dense, expected",
+    [
+        (16384, 14336, BF16, True, True, (16, 256, 2)),   # 2^24.8 dense vectors: two per thread
+        (16384, 14336, BF16, True, False, (16, 256, 1)),  # packed halves (strided)
+        (2048, 11008, F16, True, True, (16, 256, 1)),
+        (64, 14336, BF16, True, True, (16, 128, 1)),      # decode rows: 128-thread CTAs
+        (1, 14336, F16, True, True, (4, 128, 1)),         # decode-sized: two elements per thread
+        (2, 16384, F32, True, True, (4, 128, 1)),         # 2^15 elements, the limit
+        (1, 32776, BF16, True, True, (16, 128, 1)),       # just above it
+        (7, 100, BF16, True, True, (2, 256, 4)),          # 200-byte rows: element accesses
+        (8, 4096, BF16, False, True, (2, 256, 4)),        # unaligned operands
+    ],
+)
+def test_swiglu_built_in_choice(rows, f, dtype, aligned, dense, expected) -> None:
+    _native.lib().ako_b200_swiglu_set_launch(0, 0)
+    assert swiglu_plan(rows, f, dtype, aligned, dense) == expected
+
+
+def test_swiglu_override_is_followed() -> None:
+    lib = _native.lib()
+    try:
+        assert lib.ako_b200_swiglu_set_launch(64, 2) == 0
+        assert swiglu_plan(2048, 11008, BF16) == (16, 64, 2)
+        assert swiglu_plan(1, 5632, BF16) == (16, 64, 2)  # an override also skips the decode-sized path
+    finally:
+        lib.ako_b200_swiglu_set_launch(0, 0)
