@@ -49,6 +49,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr],
     ),
     "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int, _c_int]),
+    "ako_b200_rope_plan": (_c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _c_int, _c_int,
+                                    ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
+                                    ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "ako_b200_swiglu_plan": (_c_int, [ctypes.c_int64, ctypes.c_int64, _c_int, _c_int, _c_int,
                                       ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "ako_b200_rmsnorm_plan": (_c_int, [ctypes.c_int64, ctypes.c_int64, _c_int, _c_int, _c_int,

@@ -218,6 +218,10 @@ int launch_vec(const RopeArgs& a, int hpt, cudaStream_t st, const char* name) {
     }
 }
 
+// Heads per thread of the vector kernel (the measurement override, else the
+// built-in choice; see run()).
+int rope_hpt(bool interleaved) { return g_heads_per_thread > 0 ? g_heads_per_thread : (interleaved ? 2 : 1); }
+
 template <typename T>
 int run(const RopeArgs& a, bool interleaved, int access_bytes, cudaStream_t st, const char* name) {
     constexpr int VEC = 16 / sizeof(T);
@@ -226,7 +230,7 @@ int run(const RopeArgs& a, bool interleaved, int access_bytes, cudaStream_t st, 
     // positions): neox is fastest with one (3-4.5% over two at full size,
     // more for decode grids); interleaved with two (17-20% over one), whose
     // four 16-byte accesses per thread then sit a warp width apart.
-    const int hpt = g_heads_per_thread > 0 ? g_heads_per_thread : (interleaved ? 2 : 1);
+    const int hpt = rope_hpt(interleaved);
     // A thread rotates NP pairs of a head with two accesses of access_bytes:
     // one in each half (neox) or two chunks a head's thread count apart
     // (interleaved). 16-byte accesses where every operand allows them, else
@@ -318,7 +322,7 @@ bool access_ok(const RopeArgs& a, int64_t half, int es, bool interleaved, int by
 // In CUDA graphs on B200 this took 8-head decode calls (batch 8 and 32, one
 // position) from 1.34 to 1.13 and 1.23 us; 32-head calls are slower that way
 // (four passes of 8 heads) and keep the widest access.
-int access_bytes(const RopeArgs& a, int64_t half, int es, bool interleaved) {
+int access_bytes_for(const RopeArgs& a, int64_t half, int es, bool interleaved) {
     const int heads = a.t0.heads + a.t1.heads;
     const int64_t elems = a.n_pos * heads * half * 2;
     const int np4 = 4 / es;
@@ -336,7 +340,7 @@ int dispatch(RopeArgs& a, const RopeCall& c, void* stream, const char* name) {
     a.n_pos = c.batch * c.seq;
     a.seq = FastDiv::make(static_cast<uint32_t>(c.seq));
     const bool il = c.style == AKO_B200_ROPE_INTERLEAVED;
-    const int bytes = access_bytes(a, c.half, es, il);
+    const int bytes = access_bytes_for(a, c.half, es, il);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (c.dtype) {
         case AKO_B200_F32: return run<float>(a, il, bytes, st, name);
@@ -397,6 +401,53 @@ extern "C" int ako_b200_rope_qk(const void* q, int64_t q_stride_b, int64_t q_str
     a.sin = sin;
     a.ts = table_row_stride;
     return dispatch(a, c, stream, "rope_qk");
+}
+
+extern "C" int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_heads, int64_t head_dim, int style,
+                                  int dtype, int* access_bytes, int* heads_per_thread, int* block_x, int* block_y,
+                                  int* block_z) {
+    clear_error();
+    const char* op = "ako_b200_rope_plan";
+    if (access_bytes == nullptr || heads_per_thread == nullptr || block_x == nullptr || block_y == nullptr ||
+        block_z == nullptr)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null output pointer", op);
+    const int es = dtype_size(dtype);
+    if (es == 0) return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype code %d", op, dtype);
+    if (batch < 1 || seq_len < 1 || n_heads < 1 || head_dim < 2 || head_dim % 2 != 0 || n_heads > INT_MAX ||
+        head_dim > INT_MAX)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: invalid shape", op);
+    if (style != AKO_B200_ROPE_NEOX && style != AKO_B200_ROPE_INTERLEAVED)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: unknown style %d", op, style);
+    // A contiguous (batch, seq_len, heads, head_dim) tensor and tables at
+    // 256-byte aligned addresses, which are only compared, never read.
+    RopeArgs a{};
+    const uintptr_t base = 256;
+    a.t0 = RopeTensor{reinterpret_cast<const void*>(base), seq_len * n_heads * head_dim, n_heads * head_dim, head_dim,
+                      reinterpret_cast<void*>(base), seq_len * n_heads * head_dim, n_heads * head_dim, head_dim,
+                      static_cast<int>(n_heads)};
+    a.t1 = RopeTensor{nullptr, 0, 0, 0, nullptr, 0, 0, 0, 0};
+    a.cos = reinterpret_cast<const float*>(base);
+    a.sin = reinterpret_cast<const float*>(base);
+    a.ts = head_dim / 2;
+    a.n_pos = batch * seq_len;
+    a.half = static_cast<int>(head_dim / 2);
+    const bool il = style == AKO_B200_ROPE_INTERLEAVED;
+    const int bytes = access_bytes_for(a, a.half, es, il);
+    const int heads = static_cast<int>(n_heads);
+    dim3 block;
+    int hpt = 1;
+    if (bytes > 0) {
+        hpt = rope_hpt(il);
+        block = rope_block(a.half / (bytes / es), (heads + hpt - 1) / hpt, a.n_pos);
+    } else {
+        block = rope_block(a.half < 256 ? a.half : 256, heads, a.n_pos);
+    }
+    *access_bytes = bytes > 0 ? bytes : es;
+    *heads_per_thread = hpt;
+    *block_x = static_cast<int>(block.x);
+    *block_y = static_cast<int>(block.y);
+    *block_z = static_cast<int>(block.z);
+    return AKO_B200_OK;
 }
 
 extern "C" int ako_b200_rope_set_launch(int heads_per_thread) {

@@ -218,6 +218,19 @@ int ako_b200_take_device_status(int* status);
 int ako_b200_rope_set_launch(int heads_per_thread);
 
 /*
+ * The launch a RoPE call on contiguous (batch, seq_len, n_heads, head_dim)
+ * tensors and tables would get, without launching anything (host only; no
+ * GPU needed): bytes per access of x (16, 8 or 4; the element size for the
+ * pair-per-thread kernel), heads per thread, and the CTA's (x, y, z) extent
+ * (threads per head row, head groups, positions). `style` is an
+ * ako_b200_rope_style. Follows the built-in choice and any measurement
+ * override in force. Not part of the reference's interface; it has no
+ * counterpart there.
+ */
+int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_heads, int64_t head_dim, int style, int dtype,
+                       int* access_bytes, int* heads_per_thread, int* block_x, int* block_y, int* block_z);
+
+/*
  * Launch-shape override for measurement sweeps: SwiGLU CTAs of `threads`
  * threads (64, 128 or 256), each keeping `vectors_per_thread` 16-byte vectors
  * in flight (1, 2; 4 with 256 threads); (0, 0) restores the built-in choice.

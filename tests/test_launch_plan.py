@@ -1,15 +1,16 @@
-"""Host-side launch choices of the RMSNorm and SwiGLU entry points (no GPU
-needed).
+"""Host-side launch choices of the RMSNorm, RoPE and SwiGLU entry points (no
+GPU needed).
 
-``ako_b200_rmsnorm_plan`` and ``ako_b200_swiglu_plan`` report the kernel and
-launch shape a call would get from the built-in choice, through the same code
-the launch takes. These cases pin the measured rules: for RMSNorm the tables
+``ako_b200_rmsnorm_plan``, ``ako_b200_rope_plan`` and ``ako_b200_swiglu_plan``
+report the kernel and launch shape a call would get from the built-in choice,
+through the same code the launch takes. These cases pin the measured rules: for RMSNorm the tables
 for the benchmark's widths, fitted thread counts for widths that are not a
 power of two of 16-byte vectors, a warp per row for narrow rows in bulk,
 clusters for decode and for 65536-wide fused rows, the staged and chunked
 persistent kernels for wide plain 16-bit rows, and the any-width kernel for
-unaligned calls; for SwiGLU the access width, CTA size and vectors per thread
-by problem size and layout.
+unaligned calls; for RoPE the access width (with the 4-byte rule for 8-head
+decode calls), heads per thread and CTA extent; for SwiGLU the access width,
+CTA size and vectors per thread by problem size and layout.
 """
 
 from __future__ import annotations
@@ -143,3 +144,46 @@ def test_swiglu_override_is_followed() -> None:
         assert swiglu_plan(1, 5632, BF16) == (16, 64, 2)  # an override also skips the decode-sized path
     finally:
         lib.ako_b200_swiglu_set_launch(0, 0)
+
+
+def rope_plan(b: int, s: int, h: int, d: int, style: int, dtype: int) -> tuple[int, int, int, int, int]:
+    out = [ctypes.c_int() for _ in range(5)]
+    rc = _native.lib().ako_b200_rope_plan(b, s, h, d, style, dtype, *(ctypes.byref(o) for o in out))
+    assert rc == 0, _native.lib().ako_b200_last_error()
+    return tuple(o.value for o in out)
+
+
+NEOX, INTERLEAVED = 0, 1
+
+
+@pytest.mark.parametrize(
+    "shape, style, dtype, expected",
+    [
+        ((32, 4096, 32, 128), NEOX, BF16, (16, 1, 8, 32, 1)),        # config 3 q: 8 threads per head row
+        ((32, 4096, 8, 128), NEOX, BF16, (16, 1, 8, 8, 4)),          # config 3 k: 4 positions per CTA
+        ((8, 512, 32, 128), INTERLEAVED, BF16, (16, 2, 8, 16, 2)),   # interleaved: two heads per thread
+        ((16, 4096, 32, 128), NEOX, F32, (16, 1, 16, 16, 1)),
+        ((1, 1, 32, 128), NEOX, BF16, (16, 1, 8, 32, 1)),            # 32-head decode keeps 16 bytes
+        ((8, 1, 8, 128), NEOX, BF16, (4, 1, 32, 8, 1)),              # 8-head decode: 4-byte accesses
+        ((32, 1, 8, 128), NEOX, F16, (4, 1, 32, 8, 1)),
+        ((1, 1, 8, 128), NEOX, F32, (16, 1, 16, 8, 1)),              # fp32: 4 bytes is one element
+        ((8, 512, 32, 100), NEOX, BF16, (4, 1, 25, 10, 1)),          # half of 50: 4-byte accesses
+        ((8, 512, 32, 98), NEOX, BF16, (2, 1, 49, 5, 1)),            # odd half: a pair per thread
+    ],
+)
+def test_rope_built_in_choice(shape, style, dtype, expected) -> None:
+    _native.lib().ako_b200_rope_set_launch(0)
+    assert rope_plan(*shape, style, dtype) == expected
+
+
+def test_rope_override_and_errors() -> None:
+    lib = _native.lib()
+    try:
+        assert lib.ako_b200_rope_set_launch(2) == 0
+        assert rope_plan(32, 4096, 32, 128, NEOX, BF16) == (16, 2, 8, 16, 2)
+    finally:
+        lib.ako_b200_rope_set_launch(0)
+    out = [ctypes.c_int() for _ in range(5)]
+    assert lib.ako_b200_rope_plan(1, 1, 8, 127, NEOX, BF16, *(ctypes.byref(o) for o in out)) == 1
+    assert lib.ako_b200_rope_plan(1, 1, 8, 128, 5, BF16, *(ctypes.byref(o) for o in out)) == 1
+    assert lib.ako_b200_rope_plan(1, 1, 8, 128, NEOX, 9, *(ctypes.byref(o) for o in out)) == 2
