@@ -310,6 +310,39 @@ def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
             assert (int(m.group(3)), int(m.group(1)), int(m.group(2))) == (cluster, tpr, nv), (rows, h, got[:300])
         del x
 
+    # SwiGLU: swiglu_kernel<T, VEC, UNROLL, FLAT, NARROW, THREADS>
+    for rows, f, dt, packed in ((16384, 14336, torch.bfloat16, False), (16384, 14336, torch.bfloat16, True),
+                                (64, 14336, torch.float16, False), (1, 14336, torch.float16, False),
+                                (7, 100, torch.bfloat16, False)):
+        out = [ctypes.c_int() for _ in range(3)]
+        assert lib.ako_b200_swiglu_plan(rows, f, codes[dt], 1, int(not packed), *(ctypes.byref(o) for o in out)) == 0
+        access, threads, unroll = (o.value for o in out)
+        both = torch.randn(rows, 2 * f, device=cuda_device).to(dt)
+        g, u = (both[:, :f], both[:, f:]) if packed else (both[:, :f].contiguous(), both[:, f:].contiguous())
+        got = _kernel_names(lambda: kernels.swiglu_cuda_sm100(g, u))
+        m = re.search(r"swiglu_kernel<[^,]+, (\d+), (\d+), (?:true|false|1|0), (?:true|false|1|0), (\d+)>", got)
+        assert m is not None, got[:300]
+        es = torch.tensor([], dtype=dt).element_size()
+        assert (int(m.group(1)) * es, int(m.group(3)), int(m.group(2))) == (access, threads, unroll), (rows, f, got[:300])
+
+    # RoPE: rope_vec_kernel<T, NP, INTERLEAVED, HPT>, or the pair-per-thread kernel
+    from ako_b200.dispatch import references as refs
+
+    for b, sq, hh, d, style in ((32, 512, 32, 128, "neox"), (8, 1, 8, 128, "neox"), (1, 1, 32, 128, "neox"),
+                                (8, 64, 32, 128, "interleaved"), (8, 64, 8, 98, "neox")):
+        out = [ctypes.c_int() for _ in range(5)]
+        assert lib.ako_b200_rope_plan(b, sq, hh, d, 0 if style == "neox" else 1, 2, *(ctypes.byref(o) for o in out)) == 0
+        access, hpt = out[0].value, out[1].value
+        x = torch.randn(b, sq, hh, d, device=cuda_device).to(torch.bfloat16)
+        cos, sin = refs.build_rope_tables(sq, d, device=cuda_device)
+        got = _kernel_names(lambda: kernels.rope_cuda_sm100(x, cos, sin, style))
+        if d % 4 == 0:
+            m = re.search(r"rope_vec_kernel<[^,]+, (\d+), (?:true|false|1|0), (\d+)>", got)
+            assert m is not None, got[:300]
+            assert (int(m.group(1)) * 2, int(m.group(2))) == (access, hpt), (b, sq, hh, d, style, got[:300])
+        else:
+            assert "rope_scalar_kernel" in got and access == 2, got[:300]
+
 
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
