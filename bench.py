@@ -264,7 +264,10 @@ def run_reference(args) -> None:
     if op != "rmsnorm_residual":
         raise SystemExit("--impl reference supports the rmsnorm_residual workloads")
     b = 2
-    rows = max(1, min(m, (64 << 20) // (4 * h * b)))  # ~64 MB of traffic per step
+    # ~256 MB of traffic per step, the cpu_baseline leg's sample: smaller
+    # steps spend a larger share on starting the threads and touching fresh
+    # output pages, which would understate the CPU's throughput.
+    rows = max(1, min(m, (256 << 20) // (4 * h * b)))
     from oracle.ako_oracle import encode
 
     rng = np.random.default_rng(0)
