@@ -114,7 +114,12 @@ rms_rows_kernel(const RmsArgs a) {
     // (the usual case) it is loaded now, next to the row, and held packed like
     // the row (4 registers per vector); other weight dtypes, and shapes whose
     // registers are better spent on occupancy, prefetch it to L1 instead.
-    constexpr bool kWeightRegs = NV <= WEIGHT_NV || THREADS * NV <= WEIGHT_CTA_VECTORS;
+    // Plain fp32 rows on the fitted 320- and 384-thread shapes also hold it:
+    // prefetched, those compiled to 32 registers and moved 2.2x the row's
+    // bytes through L2, and 32768 x 4608 timed 0.73 of peak against 1.05
+    // holding it (5120 wide 0.88 -> 1.05; 448 threads were slower holding it).
+    constexpr bool kWeightRegs = NV <= WEIGHT_NV || THREADS * NV <= WEIGHT_CTA_VECTORS ||
+                                 (sizeof(T) == 4 && !RES && (TPR & (TPR - 1)) != 0 && THREADS * NV <= 1536);
     P wv[kWeightRegs ? NV : 1];
     bool w_regs = false;
     if constexpr (kWeightRegs) {
