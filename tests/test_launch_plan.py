@@ -187,3 +187,45 @@ def test_rope_override_and_errors() -> None:
     assert lib.ako_b200_rope_plan(1, 1, 8, 127, NEOX, BF16, *(ctypes.byref(o) for o in out)) == 1
     assert lib.ako_b200_rope_plan(1, 1, 8, 128, 5, BF16, *(ctypes.byref(o) for o in out)) == 1
     assert lib.ako_b200_rope_plan(1, 1, 8, 128, NEOX, 9, *(ctypes.byref(o) for o in out)) == 2
+
+
+@pytest.mark.parametrize("dtype", (F32, F16, BF16))
+@pytest.mark.parametrize("residual", (False, True))
+def test_every_rmsnorm_plan_covers_its_row(dtype: int, residual: bool) -> None:
+    """Over every 16-byte-aligned width up to 65536 and a spread of row counts,
+    the chosen launch holds the whole row: a cluster of CTAs of threads x
+    vectors (or the persistent kernels' 1024 or 256 threads) spans at least
+    the row's 16-byte vectors, and a row-resident CTA has at most 1024
+    threads. (A shape that fell short would leave the row's tail unwritten.)"""
+    vec = 4 if dtype == F32 else 8
+    for rows in (1, 8, 33, 64, 65, 512, 513, 1024, 8192, 16384, 40000):
+        for h in range(vec, 65536 + 1, vec):
+            kernel, cluster, threads, vectors = plan(rows, h, dtype, residual)
+            nvec = h // vec
+            if kernel == GENERIC:
+                continue
+            assert cluster * threads * vectors >= nvec, (rows, h, kernel, cluster, threads, vectors)
+            assert threads <= 1024 and cluster in (1, 2, 4, 8)
+            if kernel in (STAGED, CHUNKED):
+                assert not residual or kernel == STAGED
+                assert cluster == 1
+
+
+@pytest.mark.parametrize("dtype", (F32, F16, BF16))
+def test_every_rope_plan_fits_its_kernel(dtype: int) -> None:
+    """Over every even head size up to 512, a spread of head counts and
+    position counts, and both styles: the CTA stays within the kernels'
+    256-thread launch bound, and in the vector kernel a head row's threads
+    times the pairs each rotates per half equal the half head size."""
+    es = 4 if dtype == F32 else 2
+    for d in range(2, 513, 2):
+        for heads in (1, 3, 8, 32, 40, 64):
+            for b, s in ((1, 1), (8, 1), (2, 37), (4, 4096)):
+                for style in (NEOX, INTERLEAVED):
+                    access, hpt, bx, by, bz = rope_plan(b, s, heads, d, style, dtype)
+                    assert 1 <= bx * by * bz <= 256, (d, heads, b, s, style)
+                    assert bz <= b * s and by * hpt >= 1
+                    if access // es >= 2:  # the vector kernel (the pair-per-thread kernel loops over the row)
+                        assert bx * (access // es) == d // 2, (d, heads, b, s, style, access, bx)
+                    else:
+                        assert access == es and bx == min(d // 2, 256), (d, heads, b, s, style, access, bx)
