@@ -233,6 +233,94 @@ __device__ __forceinline__ float tree_sum(float (&v)[N]) {
     return v[0];
 }
 
+// ----------------------------------------- fixed-order sums of a row's vectors
+// The RMSNorm kernels sum a row's squares in one order that depends only on
+// the row width, never on the launch shape or the number of rows:
+//   1. each 16-byte vector's squares pairwise (tree_sum<VEC>);
+//   2. each group of 32 consecutive vectors by a fold: pairs 16 apart, then
+//      8, 4, 2, 1 (what an xor butterfly over the 32 lanes that loaded the
+//      group computes, bit for bit in every lane, since fp32 addition is
+//      commutative);
+//   3. the row's group sums by the same fold over group indices, padded with
+//      zeros to a power of two (adding +0 to a sum of squares is exact, so
+//      any padding gives the same bits).
+// Every launch shape whose thread count per row is a multiple of 32 maps a
+// group onto the 32 lanes of one warp: lane l of warp w holds, as its j-th
+// vector, vector 32 (j W + w) + l of the row (W warps per row).
+
+constexpr int ilog2_const(int n) { return n <= 1 ? 0 : 1 + ilog2_const(n / 2); }
+
+// Folds each of this lane's NV group partials (p[j]: its vector of group j)
+// across the warp. Reduce-scatter: at each of the first log2(NV) levels a lane
+// keeps half of its groups and sends the other half to its partner, so the
+// warp issues NV - 1 + 5 - log2(NV) shuffles instead of 5 NV. Returns the
+// sum of group j = lane >> (5 - log2 NV); lanes with equal top log2(NV) bits
+// hold the same bits.
+template <int NV>
+__device__ __forceinline__ float fold_groups_scatter(float (&p)[NV]) {
+    constexpr int L = ilog2_const(NV);
+    static_assert((1 << L) == NV && NV <= 32, "NV must be a power of two <= 32");
+    const int lane = static_cast<int>(threadIdx.x & 31);
+#pragma unroll
+    for (int lev = 0; lev < L; ++lev) {
+        const int off = 16 >> lev;
+        const int n = NV >> (lev + 1);
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < n; ++i) {
+            const float send = upper ? p[i] : p[i + n];
+            const float keep = upper ? p[i + n] : p[i];
+            p[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+        }
+    }
+    float v = p[0];
+#pragma unroll
+    for (int off = 16 >> L; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// Row sum for a warp that holds a whole row (groups 0..NV-1): the scatter
+// leaves group j in lanes whose top log2(NV) bits are j, so folding over
+// groups is the butterfly over those bits (offsets 16 down to 32 / NV).
+template <int NV>
+__device__ __forceinline__ float warp_row_sum(float (&p)[NV]) {
+    float v = fold_groups_scatter<NV>(p);
+#pragma unroll
+    for (int off = 16; off >= (32 >> ilog2_const(NV)); off >>= 1)
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// Stores this warp's NV group sums (from fold_groups_scatter) at group index
+// j * warps + warp of `gsum`, one lane per group.
+template <int NV>
+__device__ __forceinline__ void store_group_sums(float v, float* gsum, int warps) {
+    constexpr int L = ilog2_const(NV);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    if ((lane & ((32 >> L) - 1)) == 0) gsum[(lane >> (5 - L)) * warps + static_cast<int>(threadIdx.x >> 5)] = v;
+}
+
+// Fold of `n` group sums (n <= 32 K) read by `load(i)`, in every lane of the
+// calling warp: lane l folds its values l + 32 k over k (offsets K/2 .. 1,
+// i.e. group offsets 16 K .. 32), then the warp butterflies (16 .. 1).
+template <int K, typename Load>
+__device__ __forceinline__ float fold_group_sums(int n, Load load) {
+    static_assert((K & (K - 1)) == 0, "K must be a power of two");
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    float v[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < n ? load(i) : 0.0f;
+    }
+#pragma unroll
+    for (int off = K / 2; off > 0; off >>= 1) {
+#pragma unroll
+        for (int i = 0; i < off; ++i) v[i] = __fadd_rn(v[i], v[i + off]);
+    }
+    return warp_sum(v[0]);
+}
+
 // Sum over a CTA of THREADS threads; every thread returns the same value
 // (warp partials are combined pairwise in a fixed order). `scratch` holds
 // THREADS/32 floats of shared memory and is used once per launch.

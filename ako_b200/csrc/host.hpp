@@ -1,11 +1,24 @@
 // Host-side helpers shared by the C-ABI entry points: per-thread error text,
-// launch checking and alignment tests.
+// launch checking, alignment tests, the persistent kernels' status word, and
+// the launch overrides of measurement builds.
 #pragma once
 
 #include <cstdint>
 #include <cuda_runtime.h>
 
 #include "ako_b200.h"
+
+// Launch overrides (forced shapes, kernels, programmatic launch, wait limits)
+// exist only in the measurement build of the library (libako_b200_measure.so,
+// compiled with AKO_B200_MEASUREMENT, setters in ako_b200_measure.h). The
+// product library compiles each override as a constant at its built-in
+// value, so no call can change which kernel another caller's call runs.
+#ifdef AKO_B200_MEASUREMENT
+#include "ako_b200_measure.h"
+#define AKO_B200_OVERRIDE
+#else
+#define AKO_B200_OVERRIDE constexpr
+#endif
 
 namespace ako_b200 {
 
@@ -23,6 +36,19 @@ int sm_count();
 
 // Whether launches carry programmatic stream serialization (see launch_ex).
 bool pdl_enabled();
+
+// Host-mapped status word of the persistent RMSNorm kernels, allocated
+// (pinned, mapped, portable to every device) on first use; nullptr if that
+// allocation failed, with the error recorded. A kernel whose bounded wait
+// for a bulk copy runs out stores kStatusWaitTimeout there with a plain
+// system-scope store; the host reads it without synchronizing.
+int* device_status_word();
+
+// AKO_B200_ERR_WAIT_EXPIRED (with a message naming `op`) while the status
+// word holds an unreported expiry, else AKO_B200_OK. Every entry point that
+// launches checks it first, so an expiry is never followed silently by more
+// work; ako_b200_take_device_status clears it.
+int refuse_if_wait_expired(const char* op);
 
 // Launches kernel(a) on `grid` x `block` with `smem` bytes of dynamic shared
 // memory, in clusters of `cluster` CTAs along x when cluster > 1. With

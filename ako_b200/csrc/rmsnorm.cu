@@ -12,14 +12,19 @@ struct Shape {
     int cluster, tpr, nv;
 };
 
-Shape g_override = {0, 0, 0};
+// Launch-shape override ({0, 0, 0}: the built-in table). Measurement builds only.
+AKO_B200_OVERRIDE Shape g_override = {0, 0, 0};
 
 // Staging mode: 0 = built-in choice, 1 = row-resident kernel only,
 // 2 = staged (bulk-copy ring) kernel where it applies, 3 = chunked kernel
-// where it applies (plain rows of 2049-8192 vectors).
-int g_mode = 0;
-int g_stages = 0;
-int g_ctas_per_sm = 0;
+// where it applies (plain rows of 2049-8192 vectors). Measurement builds only.
+AKO_B200_OVERRIDE int g_mode = 0;
+AKO_B200_OVERRIDE int g_stages = 0;
+AKO_B200_OVERRIDE int g_ctas_per_sm = 0;
+
+// Polls of a persistent kernel's bounded wait for a bulk copy (measurement
+// builds can lower it to exercise the expiry path).
+AKO_B200_OVERRIDE uint32_t g_wait_polls = kWaitPolls;
 
 // Rows from which plain 16-bit rows of 2049-4096 vectors take the staged kernel.
 constexpr int64_t kStagedMinRows = 1024;
@@ -92,9 +97,13 @@ Shape fit_threads(Shape s, int64_t nvec) {
     return s;
 }
 
+// A thread-block cluster splits a row into equal slices of whole 32-vector
+// groups, so the fixed summation order sees the same groups as in one CTA.
+bool cluster_splits(int64_t nvec, int cluster) { return cluster == 1 || nvec % (32 * cluster) == 0; }
+
 bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
     const Shape& o = g_override;
-    if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && nvec % o.cluster == 0) {
+    if (o.tpr > 0 && static_cast<int64_t>(o.cluster) * o.tpr * o.nv >= nvec && cluster_splits(nvec, o.cluster)) {
         *out = o;
         return true;
     }
@@ -108,13 +117,19 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
         *out = Shape{1, tpr, 1};
         return true;
     }
-    if (nvec > 1024 && nvec <= 2048 && nvec % 4 == 0 && rows <= 64) {
+    if (nvec > 1024 && nvec <= 2048 && cluster_splits(nvec, 4) && rows <= 64) {
         *out = rows <= 32 ? Shape{4, 512, 1} : Shape{4, 256, 2};
         return true;
     }
-    if (nvec > 2048 && nvec <= 4096 && nvec % 8 == 0 && rows <= 64) {
-        *out = rows <= 8 ? Shape{8, 256, 2} : Shape{4, 512, 2};
-        return true;
+    if (nvec > 2048 && nvec <= 4096 && rows <= 64) {
+        if (rows <= 8 && cluster_splits(nvec, 8)) {
+            *out = Shape{8, 256, 2};
+            return true;
+        }
+        if (cluster_splits(nvec, 4)) {
+            *out = Shape{4, 512, 2};
+            return true;
+        }
     }
     // Narrow rows in bulk: a warp per row (four rows per 128-thread CTA)
     // with 4 or 8 vectors a thread beats a 64-thread CTA per row, whose tiny
@@ -153,7 +168,7 @@ bool pick_shape(int64_t nvec, int64_t rows, bool residual, int es, Shape* out) {
         // Rows of 4097-8192 vectors: the fused form splits them over a cluster
         // of 8 CTAs of 256 threads x 4 vectors (0.92 of peak, 0.76 with 512 x 2);
         // plain rows stay in one CTA of 1024 threads x 8 vectors.
-        if (residual && nvec % 8 == 0) {
+        if (residual && cluster_splits(nvec, 8)) {
             *out = Shape{8, 256, 4};
             return true;
         }
@@ -193,7 +208,7 @@ Plan plan_for(const RmsArgs& a, int dtype, bool res, bool vector_ok) {
 template <typename T, bool RES>
 int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
     if (vector_ok && !RES && use_chunked(a, dtype_code<T>())) {
-        const int rc = launch_rms_chunked(a, dtype_code<T>(), st);
+        const int rc = launch_rms_chunked(a, dtype_code<T>(), g_wait_polls, st);
         if (rc >= 0) return rc;
     }
     if (vector_ok && use_staged(a, sizeof(T), RES)) {
@@ -201,7 +216,7 @@ int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
         const bool chosen = g_mode == 0;  // the built-in choice above
         const int stages = g_stages > 0 ? g_stages : chosen ? 1 : 4;
         const int ctas = g_ctas_per_sm > 0 ? g_ctas_per_sm : chosen ? 1 : 2;
-        const int rc = launch_rms_staged(a, dtype, RES, stages, ctas, st);
+        const int rc = launch_rms_staged(a, dtype, RES, stages, ctas, g_wait_polls, st);
         if (rc >= 0) return rc;
     }
     if (vector_ok) {
@@ -266,6 +281,7 @@ extern "C" int ako_b200_rmsnorm(const void* x, int64_t x_row_stride, const void*
     const char* op = "ako_b200_rmsnorm";
     int rc = check_common(op, n_rows, hidden_dim, dtype, weight_dtype);
     if (rc) return rc;
+    if ((rc = refuse_if_wait_expired(op))) return rc;
     if (n_rows == 0) return AKO_B200_OK;
     if ((rc = check_operand(op, "x", x, x_row_stride, n_rows, hidden_dim))) return rc;
     if ((rc = check_operand(op, "y", y, y_row_stride, n_rows, hidden_dim))) return rc;
@@ -287,6 +303,7 @@ extern "C" int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride, co
     const char* op = "ako_b200_rmsnorm_residual";
     int rc = check_common(op, n_rows, hidden_dim, dtype, weight_dtype);
     if (rc) return rc;
+    if ((rc = refuse_if_wait_expired(op))) return rc;
     if (n_rows == 0) return AKO_B200_OK;
     if ((rc = check_operand(op, "x", x, x_row_stride, n_rows, hidden_dim))) return rc;
     if ((rc = check_operand(op, "residual", residual, residual_row_stride, n_rows, hidden_dim))) return rc;
@@ -306,6 +323,7 @@ extern "C" int ako_b200_rmsnorm_residual(const void* x, int64_t x_row_stride, co
     return dispatch<true>(a, dtype, vector_ok, static_cast<cudaStream_t>(stream));
 }
 
+#ifdef AKO_B200_MEASUREMENT
 extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_per_thread) {
     clear_error();
     if (cluster == 0 && threads_per_row == 0 && vectors_per_thread == 0) {
@@ -333,6 +351,7 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
     g_override = {cluster, threads_per_row, vectors_per_thread};
     return AKO_B200_OK;
 }
+#endif  // AKO_B200_MEASUREMENT
 
 extern "C" int ako_b200_rmsnorm_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int residual, int aligned,
                                      int* kernel, int* cluster, int* threads_per_row, int* vectors_per_thread) {
@@ -353,6 +372,7 @@ extern "C" int ako_b200_rmsnorm_plan(int64_t n_rows, int64_t hidden_dim, int dty
     return AKO_B200_OK;
 }
 
+#ifdef AKO_B200_MEASUREMENT
 extern "C" int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm) {
     clear_error();
     if (mode < 0 || mode > 3 || stages < 0 || stages > 8 || ctas_per_sm < 0 || ctas_per_sm > 8)
@@ -365,8 +385,9 @@ extern "C" int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_s
     return AKO_B200_OK;
 }
 
-extern "C" int ako_b200_take_device_status(int* status) {
-    clear_error();
-    if (status == nullptr) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "status is a null pointer");
-    return take_staged_status(status);
+extern "C" unsigned ako_b200_measure_set_wait_polls(unsigned polls) {
+    const unsigned prev = g_wait_polls;
+    g_wait_polls = polls;
+    return prev;
 }
+#endif  // AKO_B200_MEASUREMENT

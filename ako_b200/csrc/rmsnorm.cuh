@@ -6,7 +6,12 @@
 //   inv = 1 / sqrt(var + eps)     (two IEEE roundings, as torch.rsqrt on CPU)
 //   y   = round_T((v * inv) * w)  (two fp32 roundings, in the reference order)
 // Squares are rounded before they are summed (the reference materializes
-// x.pow(2)); only the summation order differs from the reference.
+// x.pow(2)); only the summation order differs from the reference. The
+// vector kernels share one summation order that depends only on the row
+// width (common.cuh, "fixed-order sums"), so a row's output bits do not
+// depend on the launch shape or on how many rows the call has: a token
+// normalized in a prefill batch and alone in a decode step gives the same
+// bits.
 //
 // Two kernels:
 //  * rms_rows_kernel: row-resident. TPR threads own a row; each thread holds
@@ -54,9 +59,12 @@ __device__ __forceinline__ float rms_inv(float total, const RmsArgs& a) {
 
 template <int TPR>
 struct RmsShape {
+    static_assert(TPR % 32 == 0, "a row's threads must be whole warps (fixed summation order)");
     static constexpr int kThreads = TPR <= 32 ? 128 : TPR;
     static constexpr int kRowsPerCta = kThreads / TPR;
 };
+
+constexpr int pow2_ceil(int n) { return n <= 1 ? 1 : 2 * pow2_ceil((n + 1) / 2); }
 
 // The weight is held in registers (4 per vector) by shapes with at most
 // WEIGHT_NV vectors per thread, or at most WEIGHT_CTA_VECTORS vectors per
@@ -86,9 +94,11 @@ rms_rows_kernel(const RmsArgs a) {
     constexpr int THREADS = RmsShape<TPR>::kThreads;
     constexpr int ROWS = RmsShape<TPR>::kRowsPerCta;
     static_assert(CLUSTER == 1 || ROWS == 1, "clusters split CTA-per-row shapes only");
+    constexpr int WARPS = THREADS / 32;
+    // Group sums of the CTA's row slice (CTA-per-row shapes): NV per warp.
+    constexpr int GROUPS = TPR > 32 ? NV * WARPS : 1;
     using P = Packed<T, VEC>;
-    __shared__ float scratch[THREADS / 32 > 0 ? THREADS / 32 : 1];
-    __shared__ float cluster_part;
+    __shared__ float gsum[GROUPS];
     pdl_enter();
 
     const int lane = threadIdx.x % TPR;
@@ -167,8 +177,8 @@ rms_rows_kernel(const RmsArgs a) {
         }
     }
 
-    // Squares are rounded, then summed pairwise: within a vector, across the
-    // thread's vectors, across lanes, across warps.
+    // Squares are rounded, then summed in the fixed order: within a vector,
+    // across each 32-vector group's lanes, across the groups.
     float part[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -182,25 +192,30 @@ rms_rows_kernel(const RmsArgs a) {
         }
         part[j] = col < width ? tree_sum<VEC>(sq) : 0.0f;
     }
-    const float acc = tree_sum<NV>(part);
     float total;
     if constexpr (TPR <= 32) {
-        total = warp_sum<TPR>(acc);
+        total = warp_row_sum<NV>(part);
     } else {
-        total = block_sum<THREADS>(acc, scratch);
-    }
-    if constexpr (CLUSTER > 1) {
-        // Publish this slice's sum, then every CTA adds the CLUSTER partials
-        // pairwise in rank order (identical result in all CTAs). The second
-        // barrier is split: arrive now, wait before exit, so no CTA leaves
-        // while another may still read its shared memory.
-        if (threadIdx.x == 0) cluster_part = total;
-        cluster_sync_all();
-        float parts[CLUSTER];
-#pragma unroll
-        for (int r = 0; r < CLUSTER; ++r) parts[r] = ld_dsmem_f32(&cluster_part, r);
-        total = tree_sum<CLUSTER>(parts);
-        cluster_arrive();
+        // Every warp folds the row's group sums itself, so no second barrier
+        // or broadcast is needed.
+        constexpr int K = pow2_ceil((CLUSTER * GROUPS + 31) / 32);
+        store_group_sums<NV>(fold_groups_scatter<NV>(part), gsum, WARPS);
+        if constexpr (CLUSTER == 1) {
+            __syncthreads();
+            total = fold_group_sums<K>(GROUPS, [&](int i) { return gsum[i]; });
+        } else {
+            // Group i of the row is group i % sg of the slice of CTA i / sg
+            // (the host splits rows into slices of whole 32-vector groups).
+            // The second cluster barrier is split: arrive now, wait before
+            // exit, so no CTA leaves while another may still read its shared
+            // memory.
+            const int sg = width / VEC / 32;
+            cluster_sync_all();
+            total = fold_group_sums<K>(CLUSTER * sg, [&](int i) {
+                return ld_dsmem_f32(&gsum[i % sg], static_cast<unsigned>(i / sg));
+            });
+            cluster_arrive();
+        }
     }
     const float inv = rms_inv(total, a);
 
@@ -509,22 +524,24 @@ int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
                      a, RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)");
 }
 
+// Polls of a persistent kernel's bounded wait for a bulk copy (about a
+// second of polling); when they run out the kernel gives up on its rows.
+constexpr uint32_t kWaitPolls = 1u << 24;
+
 // Persistent variant with rows staged in shared memory by bulk copies
 // (rmsnorm_tma.cu); -1 when the row is too wide for it.
-int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st);
+int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, uint32_t wait_polls,
+                      cudaStream_t st);
 
 // Plain rows of 2049-8192 vectors streamed through shared memory in one or
 // two chunks per row (rmsnorm_tma.cu); -1 for other rows.
-int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st);
+int launch_rms_chunked(const RmsArgs& a, int dtype, uint32_t wait_polls, cudaStream_t st);
 
 // Host-side shapes of the two persistent kernels (no launch): the staged
 // kernel's threads and vectors per thread (false when it does not take the
 // row), and the chunked kernel's chunks per row (0 when it does not).
 bool rms_staged_shape(int h, int es, bool res, int stages, int ctas_per_sm, int* threads_out, int* nv_out);
 int rms_chunks_for(int h, int es);
-
-// Reads and clears the staged kernels' device status word (synchronizing).
-int take_staged_status(int* status);
 
 // Instantiated once per dtype in rmsnorm_{f32,f16,bf16}.cu (compiled in parallel).
 #define AKO_RMS_DECLARE(T, KW)                                                        \

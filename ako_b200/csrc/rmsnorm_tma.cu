@@ -9,48 +9,68 @@
 // fused); all threads wait on the slot's mbarrier, read their 16-byte
 // vectors into registers, and the slot is refilled with the row `stages`
 // ahead as soon as the reduction's barrier shows every thread has read it.
-// Arithmetic and rounding are those of rms_rows_kernel; the pairwise sum of
-// squares is partitioned over THREADS threads (256, or 1024 for rows of
-// more than 2048 vectors), so fp32 results can differ from a row-resident
-// launch of another thread count in the last bits (the rounded residual is
-// identical, and a launch of the same thread layout is bit-identical).
+// Arithmetic, rounding and the fixed summation order are those of
+// rms_rows_kernel, so outputs are bit-identical to it for every thread count.
 //
 // rms_chunk_kernel (plain): rows streamed in one or two 64 KB chunks that
 // stay in shared memory for both passes; see its comment below.
 //
-// Every wait is bounded: if a copy never completes, the CTA records
-// kStatusWaitTimeout in g_tma_status, waits (bounded) for its other copies,
-// and leaves without writing the row.
+// Every wait is bounded: if a copy never completes, the CTA fills the rows
+// it has not produced with NaN, records kStatusWaitTimeout in the
+// host-mapped status word (after which every entry point refuses until
+// ako_b200_take_device_status clears it), waits (bounded) for its other
+// copies, and leaves.
 #include <climits>
 
 #include "rmsnorm.cuh"
 
 namespace ako_b200 {
 
-__device__ int g_tma_status = 0;
-
 namespace {
 
 constexpr int kTmaThreads = 256;       // rows of up to 8 x 256 vectors
 constexpr int kTmaWideThreads = 1024;  // rows of up to 8 x 1024 vectors
 constexpr int kMaxStages = 8;
-constexpr uint32_t kWaitPolls = 1u << 24;   // ~a second of polling
 constexpr uint32_t kDrainPolls = 1u << 20;
 
 struct TmaArgs {
     RmsArgs a;
     int stages;
     int stage_bytes;  // x row (+ residual row), multiple of 16
+    int* status;      // host-mapped status word
+    uint32_t wait_polls;
 };
+
+// Records a bounded wait's expiry where the host reads it without
+// synchronizing (a plain store: every writer stores the same value).
+__device__ __forceinline__ void record_wait_expiry(int* status) {
+    *reinterpret_cast<volatile int*>(status) = kStatusWaitTimeout;
+    __threadfence_system();
+}
+
+// Fills output row `row` (and its residual output when RES) with NaN, so a
+// row the CTA gives up on never holds stale memory.
+template <typename T, bool RES>
+__device__ void nan_fill_row(const RmsArgs& a, int64_t row) {
+    const T nan = from_f32<T>(__int_as_float(0x7fc00000));
+    T* y = static_cast<T*>(a.y) + row * a.sy;
+    T* ro = RES ? static_cast<T*>(a.ro) + row * a.sro : nullptr;
+    for (int c = static_cast<int>(threadIdx.x); c < a.h; c += static_cast<int>(blockDim.x)) {
+        y[c] = nan;
+        if constexpr (RES) ro[c] = nan;
+    }
+}
 
 template <typename T, int NV, bool RES, int THREADS>
 __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
     constexpr int VEC = 16 / sizeof(T);
     constexpr int WARPS = THREADS / 32;
     using P = Packed<T, VEC>;
+    constexpr int GROUPS = NV * WARPS;
+    constexpr int K = pow2_ceil((GROUPS + 31) / 32);
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ uint64_t full[kMaxStages];
-    __shared__ float scratch[2][WARPS];
+    __shared__ float gsum[2][GROUPS];
     pdl_enter();
     const RmsArgs& a = t.a;
     const int h = a.h;
@@ -82,10 +102,11 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
     for (int64_t row = first; row < a.rows; row += step, ++k) {
         const int slot = k % t.stages;
         const uint32_t phase = static_cast<uint32_t>(k / t.stages) & 1u;
-        const bool ok = mbar_wait_bounded(&full[slot], phase, kWaitPolls);
+        const bool ok = mbar_wait_bounded(&full[slot], phase, t.wait_polls);
         if (__syncthreads_or(!ok)) {
+            for (int64_t r2 = row; r2 < a.rows; r2 += step) nan_fill_row<T, RES>(a, r2);
             if (threadIdx.x == 0) {
-                atomicExch(&g_tma_status, kStatusWaitTimeout);
+                record_wait_expiry(t.status);
                 // Let the copies this CTA started land before it exits.
                 for (int j = 0; j < t.stages; ++j) {
                     const int64_t r2 = row + j * step;
@@ -136,10 +157,12 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
             }
             part[j] = col < h ? tree_sum<VEC>(sq) : 0.0f;
         }
-        float w_sum = warp_sum(tree_sum<NV>(part));
-        float* sc = scratch[k & 1];
-        if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
-        __syncthreads();  // every thread has read the slot and published its warp's sum
+        // Group sums alternate between two buffers: a warp writes this
+        // buffer again two rows on, after the next row's barrier, which every
+        // warp reaches only once it has read this row's sums.
+        float* gs = gsum[k & 1];
+        store_group_sums<NV>(fold_groups_scatter<NV>(part), gs, WARPS);
+        __syncthreads();  // every thread has read the slot and published its groups
         if (threadIdx.x == 0) {
             const int64_t next = row + static_cast<int64_t>(t.stages) * step;
             if (next < a.rows) {
@@ -147,10 +170,7 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
                 issue(slot, next);
             }
         }
-        float parts[WARPS];
-#pragma unroll
-        for (int i = 0; i < WARPS; ++i) parts[i] = sc[i];
-        const float total = tree_sum<WARPS>(parts);
+        const float total = fold_group_sums<K>(GROUPS, [&](int i) { return gs[i]; });
         const float inv = rms_inv(total, a);
         T* yr = static_cast<T*>(a.y) + row * a.sy;
 #pragma unroll
@@ -183,14 +203,16 @@ __global__ void __launch_bounds__(THREADS) rms_tma_kernel(const TmaArgs t) {
 // weights (when they have the row's dtype) are loaded into registers while
 // the row's sum is reduced, or while the previous chunk is written. Thread t
 // owns vectors t + 1024 j as in rms_rows_kernel<T, 1024, 4 * CHUNKS>, and
-// the per-thread sum is the same pairwise tree split between the chunks, so
-// the outputs are bit-identical to that kernel's.
+// the row's squares are summed in the same fixed order, so the outputs are
+// bit-identical to that kernel's.
 constexpr int kChunkSlots = 3;
 constexpr int kChunkNV = 4;  // vectors per thread per chunk
 
 struct ChunkArgs {
     RmsArgs a;
     int chunk_bytes;  // bytes of a full chunk (1024 x kChunkNV vectors)
+    int* status;      // host-mapped status word
+    uint32_t wait_polls;
 };
 
 template <typename T, int CHUNKS>
@@ -199,9 +221,12 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     constexpr int THREADS = kTmaWideThreads;
     constexpr int WARPS = THREADS / 32;
     using P = Packed<T, VEC>;
+    constexpr int NVR = CHUNKS * kChunkNV;  // vectors per thread per row
+    constexpr int GROUPS = NVR * WARPS;
+    constexpr int K = pow2_ceil((GROUPS + 31) / 32);
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ uint64_t full[kChunkSlots];
-    __shared__ float scratch[2][WARPS];
+    __shared__ float gsum[2][GROUPS];
     pdl_enter();
     const RmsArgs& a = c.a;
     const int h = a.h;
@@ -238,10 +263,10 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     // CTA started land (bounded), and reports false to all threads.
     auto arrive = [&](int64_t n) -> bool {
         const bool ok = mbar_wait_bounded(&full[n % kChunkSlots], static_cast<uint32_t>(n / kChunkSlots) & 1u,
-                                          kWaitPolls);
+                                          c.wait_polls);
         if (!__syncthreads_or(!ok)) return true;
         if (threadIdx.x == 0) {
-            atomicExch(&g_tma_status, kStatusWaitTimeout);
+            record_wait_expiry(c.status);
             for (int64_t m = n; m < issued; ++m)
                 mbar_wait_bounded(&full[m % kChunkSlots], static_cast<uint32_t>(m / kChunkSlots) & 1u, kDrainPolls);
         }
@@ -251,17 +276,19 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
     for (int64_t i = 0; i < my_rows; ++i) {
         const int64_t row = first + i * step;
         const int64_t n0 = CHUNKS * i;
-        float half[CHUNKS];
+        float part[NVR];  // vector sums, in the row's vector order q * kChunkNV + j
 #pragma unroll
         for (int q = 0; q < CHUNKS; ++q) {
-            if (!arrive(n0 + q)) return;
+            if (!arrive(n0 + q)) {
+                for (int64_t r2 = row; r2 < a.rows; r2 += step) nan_fill_row<T, false>(a, r2);
+                return;
+            }
             const T* xs = reinterpret_cast<const T*>(ring + static_cast<size_t>((n0 + q) % kChunkSlots) * c.chunk_bytes);
-            float part[kChunkNV];
 #pragma unroll
             for (int j = 0; j < kChunkNV; ++j) {
                 const int v = j * THREADS + threadIdx.x;               // vector within the chunk
                 const int col = ((q * kChunkNV + j) * THREADS + threadIdx.x) * VEC;  // element within the row
-                part[j] = 0.0f;
+                part[q * kChunkNV + j] = 0.0f;
                 if (col < h) {  // a slot holds only its chunk's bytes
                     float sq[VEC];
                     const P xv = *reinterpret_cast<const P*>(xs + v * VEC);
@@ -271,10 +298,9 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
                         sq[e] = __fmul_rn(f.x, f.x);
                         sq[e + 1] = __fmul_rn(f.y, f.y);
                     }
-                    part[j] = tree_sum<VEC>(sq);
+                    part[q * kChunkNV + j] = tree_sum<VEC>(sq);
                 }
             }
-            half[q] = tree_sum<kChunkNV>(part);
         }
         // Weights of the first chunk, loaded while the row's sum is reduced
         // (when they have the row's dtype; other weights load at use).
@@ -288,14 +314,11 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
             }
         };
         prefetch_w(0);
-        const float w_sum = warp_sum(CHUNKS == 2 ? __fadd_rn(half[0], half[CHUNKS - 1]) : half[0]);
-        float* sc = scratch[i & 1];
-        if ((threadIdx.x & 31) == 0) sc[threadIdx.x >> 5] = w_sum;
+        // Group sums alternate between two buffers (see rms_tma_kernel).
+        float* gs = gsum[i & 1];
+        store_group_sums<NVR>(fold_groups_scatter<NVR>(part), gs, WARPS);
         __syncthreads();
-        float parts[WARPS];
-#pragma unroll
-        for (int k = 0; k < WARPS; ++k) parts[k] = sc[k];
-        const float inv = rms_inv(tree_sum<WARPS>(parts), a);
+        const float inv = rms_inv(fold_group_sums<K>(GROUPS, [&](int g) { return gs[g]; }), a);
         T* yr = static_cast<T*>(a.y) + row * a.sy;
 #pragma unroll
         for (int q = 0; q < CHUNKS; ++q) {
@@ -340,11 +363,13 @@ __global__ void __launch_bounds__(kTmaWideThreads, 1) rms_chunk_kernel(const Chu
 }
 
 template <typename T, int CHUNKS>
-int launch_chunked(const RmsArgs& a, cudaStream_t st) {
+int launch_chunked(const RmsArgs& a, uint32_t wait_polls, cudaStream_t st) {
+    int* status = device_status_word();
+    if (status == nullptr) return AKO_B200_ERR_CUDA;
     // One-chunk rows get slots of their own size, which leaves the rest of
     // the SM's shared memory to L1 (the weight stays there).
     const int chunk_bytes = CHUNKS == 1 ? a.h * static_cast<int>(sizeof(T)) : kTmaWideThreads * kChunkNV * 16;
-    ChunkArgs c{a, chunk_bytes};
+    ChunkArgs c{a, chunk_bytes, status, wait_polls};
     const size_t smem = static_cast<size_t>(kChunkSlots) * chunk_bytes;
     auto kernel = rms_chunk_kernel<T, CHUNKS>;
     // Largest ring already allowed for this instantiation, per device.
@@ -368,9 +393,11 @@ int launch_chunked(const RmsArgs& a, cudaStream_t st) {
 }
 
 template <typename T, int NV, bool RES, int THREADS>
-int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
+int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, uint32_t wait_polls, cudaStream_t st) {
+    int* status = device_status_word();
+    if (status == nullptr) return AKO_B200_ERR_CUDA;
     const int row_bytes = a.h * static_cast<int>(sizeof(T));
-    TmaArgs t{a, stages, RES ? 2 * row_bytes : row_bytes};
+    TmaArgs t{a, stages, RES ? 2 * row_bytes : row_bytes, status, wait_polls};
     const size_t smem = static_cast<size_t>(stages) * t.stage_bytes;
     auto kernel = rms_tma_kernel<T, NV, RES, THREADS>;
     // Largest ring already allowed for this instantiation, per device.
@@ -402,22 +429,22 @@ int launch_one(const RmsArgs& a, int stages, int ctas_per_sm, cudaStream_t st) {
 }
 
 template <typename T, bool RES>
-int launch_dtype(const RmsArgs& a, int threads, int nv, int stages, int ctas_per_sm, cudaStream_t st) {
+int launch_dtype(const RmsArgs& a, int threads, int nv, int stages, int ctas_per_sm, uint32_t polls, cudaStream_t st) {
     if (threads == kTmaWideThreads) {
         switch (nv) {
-            case 4: return launch_one<T, 4, RES, kTmaWideThreads>(a, stages, ctas_per_sm, st);
+            case 4: return launch_one<T, 4, RES, kTmaWideThreads>(a, stages, ctas_per_sm, polls, st);
             case 8:
                 // Two rows of 8192 vectors exceed the ring's 200 KB.
                 if constexpr (RES) return -1;
-                else return launch_one<T, 8, RES, kTmaWideThreads>(a, stages, ctas_per_sm, st);
+                else return launch_one<T, 8, RES, kTmaWideThreads>(a, stages, ctas_per_sm, polls, st);
             default: return -1;
         }
     }
     switch (nv) {
-        case 1: return launch_one<T, 1, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
-        case 2: return launch_one<T, 2, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
-        case 4: return launch_one<T, 4, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
-        case 8: return launch_one<T, 8, RES, kTmaThreads>(a, stages, ctas_per_sm, st);
+        case 1: return launch_one<T, 1, RES, kTmaThreads>(a, stages, ctas_per_sm, polls, st);
+        case 2: return launch_one<T, 2, RES, kTmaThreads>(a, stages, ctas_per_sm, polls, st);
+        case 4: return launch_one<T, 4, RES, kTmaThreads>(a, stages, ctas_per_sm, polls, st);
+        case 8: return launch_one<T, 8, RES, kTmaThreads>(a, stages, ctas_per_sm, polls, st);
         default: return -1;
     }
 }
@@ -441,16 +468,18 @@ bool rms_staged_shape(int h, int es, bool res, int stages, int ctas_per_sm, int*
     return true;
 }
 
-int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, cudaStream_t st) {
+int launch_rms_staged(const RmsArgs& a, int dtype, bool res, int stages, int ctas_per_sm, uint32_t wait_polls,
+                      cudaStream_t st) {
     int threads = 0, nv = 0;
     if (!rms_staged_shape(a.h, dtype_size(dtype), res, stages, ctas_per_sm, &threads, &nv)) return -1;
+    const uint32_t p = wait_polls;
     switch (dtype) {
-        case AKO_B200_F32: return res ? launch_dtype<float, true>(a, threads, nv, stages, ctas_per_sm, st)
-                                      : launch_dtype<float, false>(a, threads, nv, stages, ctas_per_sm, st);
-        case AKO_B200_F16: return res ? launch_dtype<__half, true>(a, threads, nv, stages, ctas_per_sm, st)
-                                      : launch_dtype<__half, false>(a, threads, nv, stages, ctas_per_sm, st);
-        default: return res ? launch_dtype<__nv_bfloat16, true>(a, threads, nv, stages, ctas_per_sm, st)
-                            : launch_dtype<__nv_bfloat16, false>(a, threads, nv, stages, ctas_per_sm, st);
+        case AKO_B200_F32: return res ? launch_dtype<float, true>(a, threads, nv, stages, ctas_per_sm, p, st)
+                                      : launch_dtype<float, false>(a, threads, nv, stages, ctas_per_sm, p, st);
+        case AKO_B200_F16: return res ? launch_dtype<__half, true>(a, threads, nv, stages, ctas_per_sm, p, st)
+                                      : launch_dtype<__half, false>(a, threads, nv, stages, ctas_per_sm, p, st);
+        default: return res ? launch_dtype<__nv_bfloat16, true>(a, threads, nv, stages, ctas_per_sm, p, st)
+                            : launch_dtype<__nv_bfloat16, false>(a, threads, nv, stages, ctas_per_sm, p, st);
     }
 }
 
@@ -463,25 +492,17 @@ int rms_chunks_for(int h, int es) {
     return nvec > per_chunk ? 2 : 1;
 }
 
-int launch_rms_chunked(const RmsArgs& a, int dtype, cudaStream_t st) {
+int launch_rms_chunked(const RmsArgs& a, int dtype, uint32_t wait_polls, cudaStream_t st) {
     const int chunks = rms_chunks_for(a.h, dtype_size(dtype));
     if (chunks == 0) return -1;
     const bool two = chunks == 2;
+    const uint32_t p = wait_polls;
     switch (dtype) {
-        case AKO_B200_F32: return two ? launch_chunked<float, 2>(a, st) : launch_chunked<float, 1>(a, st);
-        case AKO_B200_F16: return two ? launch_chunked<__half, 2>(a, st) : launch_chunked<__half, 1>(a, st);
-        default: return two ? launch_chunked<__nv_bfloat16, 2>(a, st) : launch_chunked<__nv_bfloat16, 1>(a, st);
+        case AKO_B200_F32: return two ? launch_chunked<float, 2>(a, p, st) : launch_chunked<float, 1>(a, p, st);
+        case AKO_B200_F16: return two ? launch_chunked<__half, 2>(a, p, st) : launch_chunked<__half, 1>(a, p, st);
+        default:
+            return two ? launch_chunked<__nv_bfloat16, 2>(a, p, st) : launch_chunked<__nv_bfloat16, 1>(a, p, st);
     }
-}
-
-int take_staged_status(int* status) {
-    int value = 0;
-    const int zero = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&value, g_tma_status, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_tma_status, &zero, sizeof(int));
-    if (e != cudaSuccess) return set_error(AKO_B200_ERR_CUDA, "device status: %s", cudaGetErrorString(e));
-    *status = value;
-    return AKO_B200_OK;
 }
 
 }  // namespace ako_b200

@@ -45,7 +45,7 @@ struct RopeArgs {
     int half;
 };
 
-int g_heads_per_thread = 0;  // 0: built-in choice
+AKO_B200_OVERRIDE int g_heads_per_thread = 0;  // 0: built-in choice (measurement builds can force 1, 2, 4)
 
 template <int N>
 __device__ __forceinline__ void load_table(const float* p, float* out) {
@@ -364,6 +364,7 @@ extern "C" int ako_b200_rope(const void* x, int64_t x_stride_b, int64_t x_stride
     const RopeCall c{batch, seq_len, head_dim / 2, style, dtype};
     int rc = check_call(op, c, head_dim, cos, sin, table_row_stride);
     if (rc) return rc;
+    if ((rc = refuse_if_wait_expired(op))) return rc;
     if (n_heads < 0 || n_heads > INT_MAX) return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: bad n_heads", op);
     if (batch == 0 || seq_len == 0 || n_heads == 0) return AKO_B200_OK;
     RopeArgs a{};
@@ -388,6 +389,7 @@ extern "C" int ako_b200_rope_qk(const void* q, int64_t q_stride_b, int64_t q_str
     const RopeCall c{batch, seq_len, head_dim / 2, style, dtype};
     int rc = check_call(op, c, head_dim, cos, sin, table_row_stride);
     if (rc) return rc;
+    if ((rc = refuse_if_wait_expired(op))) return rc;
     if (q_heads < 0 || k_heads < 0 || q_heads + k_heads > INT_MAX)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: bad head counts", op);
     if (batch == 0 || seq_len == 0 || q_heads + k_heads == 0) return AKO_B200_OK;
@@ -450,6 +452,7 @@ extern "C" int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_head
     return AKO_B200_OK;
 }
 
+#ifdef AKO_B200_MEASUREMENT
 extern "C" int ako_b200_rope_set_launch(int heads_per_thread) {
     clear_error();
     if (heads_per_thread != 0 && heads_per_thread != 1 && heads_per_thread != 2 && heads_per_thread != 4)
@@ -458,3 +461,4 @@ extern "C" int ako_b200_rope_set_launch(int heads_per_thread) {
     g_heads_per_thread = heads_per_thread;
     return AKO_B200_OK;
 }
+#endif  // AKO_B200_MEASUREMENT

@@ -42,8 +42,10 @@ struct SwigluArgs {
 constexpr int kThreads = 256;  // default CTA size
 constexpr int64_t kTinyElements = int64_t{1} << 15;  // up to this many: 4-byte accesses
 
-int g_threads = 0;  // tuning override of the CTA size (0: built-in)
-int g_unroll = 0;   // tuning override of vectors in flight per thread (0: built-in)
+// Tuning overrides of the CTA size and of the vectors in flight per thread
+// (0: built-in choice). Measurement builds only.
+AKO_B200_OVERRIDE int g_threads = 0;
+AKO_B200_OVERRIDE int g_unroll = 0;
 
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
@@ -233,6 +235,7 @@ extern "C" int ako_b200_swiglu(const void* gate, int64_t gate_row_stride, const 
     if (n_rows == 0 || hidden_dim == 0) return AKO_B200_OK;
     if (gate == nullptr || up == nullptr || y == nullptr)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: null pointer", op);
+    if (const int rc = refuse_if_wait_expired(op)) return rc;
     if (n_rows > 1 && (gate_row_stride < hidden_dim || up_row_stride < hidden_dim || y_row_stride < hidden_dim))
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "%s: a row stride is smaller than hidden_dim %lld", op,
                          static_cast<long long>(hidden_dim));
@@ -268,6 +271,7 @@ extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtyp
     return AKO_B200_OK;
 }
 
+#ifdef AKO_B200_MEASUREMENT
 extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {
     clear_error();
     const int key = threads * 16 + vectors_per_thread;
@@ -280,3 +284,4 @@ extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {
     g_unroll = vectors_per_thread;
     return AKO_B200_OK;
 }
+#endif  // AKO_B200_MEASUREMENT

@@ -120,7 +120,7 @@ def rmsnorm_cuda_sm100(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6)
     y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     y2 = y.view(-1, hidden)
     with _DeviceGuard(x.device):
-        status = _native.lib().ako_b200_rmsnorm(
+        status = _native.active().ako_b200_rmsnorm(
             x2.data_ptr(), _row_stride(x2), weight.data_ptr(), wcode,
             y2.data_ptr(), _row_stride(y2), x2.shape[0], hidden, float(eps), code, _stream(x.device),
         )
@@ -153,7 +153,7 @@ def rmsnorm_residual_cuda_sm100(
     y2 = y.view(-1, hidden)
     ro2 = ro.view(-1, hidden)
     with _DeviceGuard(x.device):
-        status = _native.lib().ako_b200_rmsnorm_residual(
+        status = _native.active().ako_b200_rmsnorm_residual(
             x2.data_ptr(), _row_stride(x2), r2.data_ptr(), _row_stride(r2), weight.data_ptr(), wcode,
             y2.data_ptr(), _row_stride(y2), ro2.data_ptr(), _row_stride(ro2),
             x2.shape[0], hidden, float(eps), code, _stream(x.device),
@@ -182,7 +182,7 @@ def rope_cuda_sm100(
     x, y = _rope_out(x)
     batch, seq_len, n_heads, head_dim = x.shape
     with _DeviceGuard(x.device):
-        status = _native.lib().ako_b200_rope(
+        status = _native.active().ako_b200_rope(
             x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
             cos.data_ptr(), sin.data_ptr(), cos.stride(0),
             y.data_ptr(), y.stride(0), y.stride(1), y.stride(2),
@@ -245,7 +245,7 @@ def rope_qk_cuda_sm100(
     k, ko = _rope_out(k)
     batch, seq_len, qh, d = q.shape
     with _DeviceGuard(q.device):
-        status = _native.lib().ako_b200_rope_qk(
+        status = _native.active().ako_b200_rope_qk(
             q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
             k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
             cos.data_ptr(), sin.data_ptr(), cos.stride(0),
@@ -280,7 +280,7 @@ def swiglu_cuda_sm100(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     u2 = _rows_view(up.reshape(1) if up.dim() == 0 else up, hidden)
     y2 = y.view(-1, hidden)
     with _DeviceGuard(gate.device):
-        status = _native.lib().ako_b200_swiglu(
+        status = _native.active().ako_b200_swiglu(
             g2.data_ptr(), _row_stride(g2), u2.data_ptr(), _row_stride(u2),
             y2.data_ptr(), _row_stride(y2), g2.shape[0], hidden, code, _stream(gate.device),
         )

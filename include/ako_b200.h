@@ -15,10 +15,17 @@
  * `ako_b200/kernels.py`; it allocates the outputs with torch and calls these.
  *
  * Numerics follow the reference's PyTorch definitions: 16-bit inputs are
- * upcast to fp32, every intermediate is an fp32 operation rounded to nearest
- * in the reference's order (no fused multiply-add where the reference
- * rounds between a multiply and an add), and the result is rounded once to
- * the storage dtype.
+ * upcast to fp32, intermediates are fp32 operations rounded to nearest in
+ * the reference's order (no fused multiply-add where the reference rounds
+ * between a multiply and an add), and the result is rounded once to the
+ * storage dtype. Two documented departures: RMSNorm sums a row's squares in
+ * its own fixed order (see ako_b200_rmsnorm), and 16-bit SwiGLU uses the
+ * hardware exponential and reciprocal (see ako_b200_swiglu).
+ *
+ * This header is the product interface. Launch overrides for measurement
+ * (forced shapes and kernels, programmatic launch off, wait limits) exist
+ * only in the separate measurement build, libako_b200_measure.so, and are
+ * declared in ako_b200_measure.h.
  */
 #ifndef AKO_B200_H_
 #define AKO_B200_H_
@@ -40,7 +47,8 @@ typedef enum {
     AKO_B200_OK = 0,
     AKO_B200_ERR_INVALID_ARGUMENT = 1, /* shape, stride, pointer or style problem  */
     AKO_B200_ERR_UNSUPPORTED_DTYPE = 2, /* dtype code outside ako_b200_dtype        */
-    AKO_B200_ERR_CUDA = 3               /* the launch itself failed (cudaError_t)   */
+    AKO_B200_ERR_CUDA = 3,              /* the launch itself failed (cudaError_t)   */
+    AKO_B200_ERR_WAIT_EXPIRED = 4       /* refused: see ako_b200_take_device_status */
 } ako_b200_status;
 
 /* RoPE pairing conventions (reference: ako/ops/rope_ref.py:1-11). */
@@ -50,7 +58,7 @@ typedef enum {
 } ako_b200_rope_style;
 
 /* ABI version of this header; bumped on any signature change. */
-#define AKO_B200_ABI_VERSION 2
+#define AKO_B200_ABI_VERSION 3
 
 int ako_b200_abi_version(void);
 
@@ -77,6 +85,14 @@ const char* ako_b200_last_error(void);
  * n_rows == 0 is a no-op. hidden_dim >= 1. Strides >= hidden_dim when
  * n_rows > 1. Any alignment is accepted; 16-byte aligned rows use 128-bit
  * accesses.
+ *
+ * Summation order: on rows of whole 16-byte vectors (hidden_dim * element
+ * size a multiple of 16, 16-byte aligned pointers and strides) the squares
+ * are summed in one fixed order that depends only on hidden_dim: each
+ * vector's squares pairwise, each run of 32 consecutive vectors by a fold
+ * (pairs 16, 8, 4, 2, 1 apart), then the runs by the same fold. A row's
+ * output bits therefore do not depend on n_rows or on which kernel the call
+ * picks. Other rows accumulate in fp64 and round once.
  */
 int ako_b200_rmsnorm(const void* x, int64_t x_row_stride,
                      const void* weight, int weight_dtype,
@@ -151,6 +167,10 @@ int ako_b200_rope_qk(const void* q, int64_t q_stride_b, int64_t q_stride_s, int6
  * evaluated in fp32 and rounded once. gate, up and y are n_rows x hidden_dim
  * with independent row strides, so the packed layout (one [M, 2F] buffer whose
  * halves are gate and up) is passed as two strided views without a copy.
+ * fp32 uses CUDA's expf and an IEEE division. 16-bit dtypes use the hardware
+ * exponential and reciprocal: the fp32 value is within about 2.5e-6
+ * (relative) of the reference's, and the rounded output equals the
+ * reference's or one of its two neighbours.
  *
  * Replaces the `swiglu` KernelFn `fn(gate, up)`:
  *   reference ako/ops/swiglu_ref.py:16-32 (definition),
@@ -164,28 +184,6 @@ int ako_b200_swiglu(const void* gate, int64_t gate_row_stride,
                     int dtype, void* stream);
 
 /*
- * Launch-shape override for measurement sweeps: rows are split over
- * `cluster` CTAs (1, 2, 4 or 8; a thread-block cluster when > 1), each row
- * slice held by `threads_per_row` threads with `vectors_per_thread` 16-byte
- * vectors each. (0, 0, 0) restores the built-in table. A shape that cannot
- * hold a given row is ignored for that row. Not part of the reference's
- * interface; it has no counterpart there. Process-wide, not thread-safe.
- */
-int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_per_thread);
-
-/*
- * RMSNorm kernel choice for measurement sweeps: mode 1 uses the
- * row-resident kernel only; mode 2 uses, where the row fits, the persistent
- * kernel that stages rows in shared memory with 1-D bulk copies (`stages`
- * rows in flight per CTA, `ctas_per_sm` CTAs per SM; 0 = defaults); mode 3
- * uses, for plain rows of 2049-8192 16-byte vectors, the persistent kernel
- * that streams each row through shared memory in one or two chunks; mode 0
- * restores the built-in choice. Not part of the reference's interface; it
- * has no counterpart there. Process-wide, not thread-safe.
- */
-int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm);
-
-/*
  * The kernel an RMSNorm call of `n_rows` x `hidden_dim` in `dtype` would run,
  * without launching anything (host only; no GPU needed): *kernel is 0 for the
  * row-resident kernel (a thread-block cluster of *cluster CTAs, each row
@@ -193,29 +191,28 @@ int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm);
  * vectors), 1 for the staged and 2 for the chunked persistent kernel
  * (threads and vectors per thread; cluster 1), 3 for the any-width kernel.
  * `residual` selects the fused form; `aligned` says whether the call's
- * pointers and row strides are 16-byte aligned. Follows the built-in choice
- * and any measurement override in force. Not part of the reference's
- * interface; it has no counterpart there.
+ * pointers and row strides are 16-byte aligned. Follows the library's
+ * built-in choice (in the measurement build, any override in force). Not
+ * part of the reference's interface; it has no counterpart there.
  */
 int ako_b200_rmsnorm_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int residual, int aligned,
                           int* kernel, int* cluster, int* threads_per_row, int* vectors_per_thread);
 
 /*
- * Reads and clears the device status word of this library's kernels on the
- * current device: 0, or 1 when a kernel's bounded wait for an asynchronous
- * copy ran out (the kernel then left its rows unwritten). Synchronizes the
- * device; meant for diagnostics and tests. Not part of the reference's
- * interface; it has no counterpart there.
+ * Status of the persistent RMSNorm kernels (the staged and chunked kernels,
+ * which wait on 1-D bulk copies). Every such wait is bounded (about a
+ * second of polling). If one runs out, the kernel writes NaN into each
+ * output row it could not produce (y, and residual_out for the fused form),
+ * records the event in a status word in host-mapped memory, and exits. From
+ * then on every entry point of this library refuses with
+ * AKO_B200_ERR_WAIT_EXPIRED, before launching anything, so the expiry
+ * surfaces at the next call without any synchronization on the hot path.
+ * This function synchronizes the current device, stores the status in
+ * *status (0: no expiry; 1: a wait ran out) and clears it, after which calls
+ * are accepted again. Not part of the reference's interface; it has no
+ * counterpart there.
  */
 int ako_b200_take_device_status(int* status);
-
-/*
- * Launch-shape override for measurement sweeps: each RoPE thread rotates
- * `heads_per_thread` heads (1, 2 or 4); 0 restores the built-in choice. Not
- * part of the reference's interface; it has no counterpart there.
- * Process-wide, not thread-safe.
- */
-int ako_b200_rope_set_launch(int heads_per_thread);
 
 /*
  * The launch a RoPE call on contiguous (batch, seq_len, n_heads, head_dim)
@@ -223,21 +220,12 @@ int ako_b200_rope_set_launch(int heads_per_thread);
  * GPU needed): bytes per access of x (16, 8 or 4; the element size for the
  * pair-per-thread kernel), heads per thread, and the CTA's (x, y, z) extent
  * (threads per head row, head groups, positions). `style` is an
- * ako_b200_rope_style. Follows the built-in choice and any measurement
- * override in force. Not part of the reference's interface; it has no
- * counterpart there.
+ * ako_b200_rope_style. Follows the library's built-in choice (in the
+ * measurement build, any override in force). Not part of the reference's
+ * interface; it has no counterpart there.
  */
 int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_heads, int64_t head_dim, int style, int dtype,
                        int* access_bytes, int* heads_per_thread, int* block_x, int* block_y, int* block_z);
-
-/*
- * Launch-shape override for measurement sweeps: SwiGLU CTAs of `threads`
- * threads (64, 128 or 256), each keeping `vectors_per_thread` 16-byte vectors
- * in flight (1, 2; 4 with 256 threads); (0, 0) restores the built-in choice.
- * Not part of the reference's interface; it has no counterpart there.
- * Process-wide, not thread-safe.
- */
-int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
 
 /*
  * The launch a SwiGLU call of `n_rows` x `hidden_dim` in `dtype` would get,
@@ -245,23 +233,12 @@ int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
  * (16; 4 for decode-sized problems; the element size when the operands are
  * not 16-byte aligned), threads per CTA and vectors per thread. `aligned`
  * says whether the call's pointers and row strides are 16-byte aligned,
- * `dense` whether all three operands are contiguous. Follows the built-in
- * choice and any measurement override in force. Not part of the reference's
- * interface; it has no counterpart there.
+ * `dense` whether all three operands are contiguous. Follows the library's
+ * built-in choice (in the measurement build, any override in force). Not
+ * part of the reference's interface; it has no counterpart there.
  */
 int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int aligned, int dense,
                          int* access_bytes, int* threads, int* vectors_per_thread);
-
-/*
- * Programmatic dependent launch: with `enable` = 1 (the default) every
- * kernel of this library is launched with programmatic stream serialization,
- * so it may start while the previous kernel in the stream drains; it waits
- * for that kernel's completion before touching memory, so results do not
- * change. 0 launches with plain stream order. Returns the previous setting.
- * Not part of the reference's interface; it has no counterpart there.
- * Process-wide.
- */
-int ako_b200_set_pdl(int enable);
 
 #ifdef __cplusplus
 }

@@ -100,6 +100,7 @@ typedef struct {
     int64_t h;
     float eps;
     int dtype, wdtype;
+    int fixed_order; /* 1: the CUDA kernels' summation order (fixed_order_sum) */
 } rms_ctx;
 
 /* Pairwise sum of n floats (blocks of 8 summed in order). torch's CPU
@@ -113,6 +114,51 @@ static float pairwise_sum(const float* v, int64_t n) {
     }
     const int64_t m = ((n / 2) + 7) & ~(int64_t)7;
     return pairwise_sum(v, m) + pairwise_sum(v + m, n - m);
+}
+
+/* Fold of n = 2^k values in place: v[i] += v[i + n/2], then n/4, ... 1. */
+static float fold(float* v, int64_t n) {
+    for (int64_t off = n / 2; off >= 1; off /= 2)
+        for (int64_t i = 0; i < off; ++i) v[i] = v[i] + v[i + off];
+    return v[0];
+}
+
+/* The summation order of the CUDA RMSNorm kernels on rows of 16-byte
+ * vectors (`vec` elements each; ako_b200/csrc/rmsnorm.cuh, "Fixed summation
+ * order"). It is a model of the kernels, not of the reference, and depends
+ * on the row width only:
+ *   1. each vector's squares pairwise (pairs 1, 2, 4 apart);
+ *   2. each group of 32 consecutive vectors by a fold (pairs 16, 8, 4, 2, 1
+ *      apart), zeros past the row's end;
+ *   3. the groups by the same fold over group indices, zero-padded to a
+ *      power of two.
+ * Adding a zero to a sum of squares is exact, so any padding gives the same
+ * bits. */
+static float fixed_order_sum(const float* sq, int64_t h, int vec) {
+    const int64_t nvec = h / vec;
+    const int64_t groups = (nvec + 31) / 32;
+    int64_t padded = 1;
+    while (padded < groups) padded *= 2;
+    float* g = (float*)calloc((size_t)padded, sizeof(float));
+    if (!g) return NAN;
+    for (int64_t k = 0; k < groups; ++k) {
+        float lanes[32];
+        for (int l = 0; l < 32; ++l) {
+            const int64_t v = k * 32 + l;
+            lanes[l] = 0.0f;
+            if (v < nvec) {
+                float e[8];
+                for (int i = 0; i < vec; ++i) e[i] = sq[v * vec + i];
+                for (int st = 1; st < vec; st *= 2)
+                    for (int i = 0; i + st < vec; i += 2 * st) e[i] = e[i] + e[i + st];
+                lanes[l] = e[0];
+            }
+        }
+        g[k] = fold(lanes, 32);
+    }
+    const float total = fold(g, padded);
+    free(g);
+    return total;
 }
 
 /* ako/ops/rmsnorm_ref.py:8-23 and :26-50 */
@@ -131,7 +177,9 @@ static void rms_rows(const void* vctx, int64_t begin, int64_t end) {
             }
             sq[i] = v * v; /* x.pow(2), rounded per element */
         }
-        const float mean = pairwise_sum(sq, h) / (float)h;
+        const int es = c->dtype == F32 ? 4 : 2;
+        const float total = c->fixed_order ? fixed_order_sum(sq, h, 16 / es) : pairwise_sum(sq, h);
+        const float mean = total / (float)h;
         const float inv = 1.0f / sqrtf(mean + c->eps);
         for (int64_t i = 0; i < h; ++i) {
             const float v = load(c->r ? c->ro : c->x, base + i, c->dtype);
@@ -144,14 +192,25 @@ static void rms_rows(const void* vctx, int64_t begin, int64_t end) {
 
 int ako_oracle_rmsnorm(const void* x, const void* w, int wdtype, void* y, int64_t rows, int64_t h, float eps,
                        int dtype, int threads) {
-    rms_ctx c = {x, NULL, w, y, NULL, h, eps, dtype, wdtype};
+    rms_ctx c = {x, NULL, w, y, NULL, h, eps, dtype, wdtype, 0};
     parallel_rows(rms_rows, &c, rows, threads);
     return 0;
 }
 
 int ako_oracle_rmsnorm_residual(const void* x, const void* r, const void* w, int wdtype, void* y, void* ro,
                                 int64_t rows, int64_t h, float eps, int dtype, int threads) {
-    rms_ctx c = {x, r, w, y, ro, h, eps, dtype, wdtype};
+    rms_ctx c = {x, r, w, y, ro, h, eps, dtype, wdtype, 0};
+    parallel_rows(rms_rows, &c, rows, threads);
+    return 0;
+}
+
+/* Both forms with the kernels' summation order (fixed_order_sum); `r` may be
+ * NULL for plain RMSNorm. h * element size must be a multiple of 16. */
+int ako_oracle_rmsnorm_fixed_order(const void* x, const void* r, const void* w, int wdtype, void* y, void* ro,
+                                   int64_t rows, int64_t h, float eps, int dtype, int threads) {
+    const int es = dtype == F32 ? 4 : 2;
+    if ((h * es) % 16 != 0) return 1;
+    rms_ctx c = {x, r, w, y, r ? ro : NULL, h, eps, dtype, wdtype, 1};
     parallel_rows(rms_rows, &c, rows, threads);
     return 0;
 }

@@ -37,6 +37,7 @@ def lib() -> ctypes.CDLL:
         p, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
         handle.ako_oracle_rmsnorm.argtypes = [p, p, i32, p, i64, i64, f32, i32, i32]
         handle.ako_oracle_rmsnorm_residual.argtypes = [p, p, p, i32, p, p, i64, i64, f32, i32, i32]
+        handle.ako_oracle_rmsnorm_fixed_order.argtypes = [p, p, p, i32, p, p, i64, i64, f32, i32, i32]
         handle.ako_oracle_rope.argtypes = [p, p, p, p, i64, i64, i64, i64, i32, i32, i32]
         handle.ako_oracle_swiglu.argtypes = [p, p, p, i64, i64, i32, i32]
         _lib = handle
@@ -71,6 +72,24 @@ def rmsnorm_residual(x, r, w, eps, dtype, w_dtype=None, threads=None):
     return y, ro
 
 
+def rmsnorm_fixed_order(x, r, w, eps, dtype, w_dtype=None, threads=None):
+    """RMSNorm (``r`` None) or fused residual RMSNorm with the CUDA kernels'
+    summation order instead of the reference's: a model of the kernels used to
+    check them bit for bit. Returns ``y`` or ``(y, residual_out)``."""
+    x, w = _c(x), _c(w)
+    r = None if r is None else _c(r)
+    y = np.empty_like(x)
+    ro = np.empty_like(x) if r is not None else None
+    h = x.shape[-1]
+    rc = lib().ako_oracle_rmsnorm_fixed_order(
+        x.ctypes.data, None if r is None else r.ctypes.data, w.ctypes.data, _CODE[w_dtype or dtype], y.ctypes.data,
+        None if ro is None else ro.ctypes.data, x.size // h, h, float(eps), _CODE[dtype],
+        threads or default_threads())
+    if rc != 0:
+        raise ValueError(f"rmsnorm_fixed_order: rows of {h} {dtype} elements are not whole 16-byte vectors")
+    return y if r is None else (y, ro)
+
+
 def rope(x, cos, sin, style, dtype, threads=None):
     x = _c(x)
     cos = _c(cos.astype(np.float32))
@@ -91,4 +110,4 @@ def swiglu(g, u, dtype, threads=None):
     return y
 
 
-__all__ = ["build", "lib", "rmsnorm", "rmsnorm_residual", "rope", "swiglu", "storage_dtype", "default_threads"]
+__all__ = ["build", "lib", "rmsnorm", "rmsnorm_residual", "rmsnorm_fixed_order", "rope", "swiglu", "storage_dtype", "default_threads"]

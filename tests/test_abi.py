@@ -1,6 +1,7 @@
-"""The C-ABI library without a GPU: it loads, exports every symbol the header
-declares, and rejects bad arguments with the documented status codes before
-touching the device. The KernelFn wrappers refuse CPU tensors (no fallback)."""
+"""The C-ABI libraries without a GPU: each loads and exports every symbol its
+header declares (the product library none of the measurement overrides), and
+rejects bad arguments with the documented status codes before touching the
+device. The KernelFn wrappers refuse CPU tensors (no fallback)."""
 
 from __future__ import annotations
 
@@ -13,25 +14,43 @@ import torch
 
 from ako_b200 import _native, kernels
 
-HEADER = Path(__file__).resolve().parent.parent / "include" / "ako_b200.h"
+INCLUDE = Path(__file__).resolve().parent.parent / "include"
+HEADER = INCLUDE / "ako_b200.h"
+MEASURE_HEADER = INCLUDE / "ako_b200_measure.h"
+
+
+def _built() -> None:
+    if not (_native.LIB_PATH.exists() and _native.MEASURE_LIB_PATH.exists()):
+        from ako_b200.build import build
+
+        build()
 
 
 @pytest.fixture(scope="module")
 def lib():
-    if not _native.LIB_PATH.exists():
-        from ako_b200.build import build
-
-        build()
+    _built()
     return _native.lib()
 
 
-def declared_symbols() -> list[str]:
-    text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(ako_b200_\w+)\s*\(", text, re.M)))
+@pytest.fixture(scope="module")
+def mlib():
+    _built()
+    return _native.measure_lib()
 
 
-def test_header_declares_the_bound_symbols() -> None:
-    assert declared_symbols() == sorted(_native.SIGNATURES)
+def declared_symbols(header: Path = HEADER) -> list[str]:
+    text = header.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+|unsigned\s+)?\w+\*?\s+\*?(ako_b200_\w+)\s*\(", text, re.M)))
+
+
+def _exported(path: Path) -> set[str]:
+    raw = ctypes.CDLL(str(path))
+    return {n for n in [*_native.SIGNATURES, *_native.MEASURE_SIGNATURES] if hasattr(raw, n)}
+
+
+def test_headers_declare_the_bound_symbols() -> None:
+    assert declared_symbols(HEADER) == sorted(_native.SIGNATURES)
+    assert declared_symbols(MEASURE_HEADER) == sorted(_native.MEASURE_SIGNATURES)
 
 
 def test_library_exports_every_declared_symbol(lib) -> None:
@@ -40,14 +59,34 @@ def test_library_exports_every_declared_symbol(lib) -> None:
         assert hasattr(raw, name), name
 
 
-def test_abi_version(lib) -> None:
-    assert lib.ako_b200_abi_version() == _native.ABI_VERSION == 2
+def test_product_library_has_no_measurement_overrides(lib) -> None:
+    """Forced shapes, kernels, launch modes and wait limits exist only in the
+    measurement build: the product library exports none of them."""
+    assert _exported(_native.LIB_PATH) == set(_native.SIGNATURES)
+
+
+def test_measurement_library_exports_both_headers(mlib) -> None:
+    assert _exported(_native.MEASURE_LIB_PATH) == set(_native.SIGNATURES) | set(_native.MEASURE_SIGNATURES)
+    assert set(declared_symbols(HEADER)) | set(declared_symbols(MEASURE_HEADER)) <= _exported(_native.MEASURE_LIB_PATH)
+
+
+def test_abi_version(lib, mlib) -> None:
+    assert lib.ako_b200_abi_version() == mlib.ako_b200_abi_version() == _native.ABI_VERSION == 3
 
 
 def test_status_strings(lib) -> None:
     assert lib.ako_b200_status_string(0) == b"AKO_B200_OK"
     assert lib.ako_b200_status_string(3) == b"AKO_B200_ERR_CUDA"
+    assert lib.ako_b200_status_string(4) == b"AKO_B200_ERR_WAIT_EXPIRED"
     assert lib.ako_b200_status_string(99) == b"AKO_B200_ERR_UNKNOWN"
+
+
+def test_device_status_without_any_persistent_launch(lib) -> None:
+    """No persistent kernel has run in this process: the status is 0 and the
+    call needs no device."""
+    value = ctypes.c_int(7)
+    assert lib.ako_b200_take_device_status(ctypes.byref(value)) == 0 and value.value == 0
+    assert lib.ako_b200_take_device_status(None) == 1
 
 
 def test_rmsnorm_argument_errors(lib) -> None:
@@ -87,13 +126,13 @@ def test_residual_rope_swiglu_argument_errors(lib) -> None:
     assert lib.ako_b200_swiglu(None, 0, None, 0, None, 0, 0, 8, 2, None) == 0
 
 
-def test_launch_override_validation(lib) -> None:
-    assert lib.ako_b200_rmsnorm_set_launch(1, 128, 4) == 0
-    assert lib.ako_b200_rmsnorm_set_launch(4, 128, 4) == 0
-    assert lib.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_launch(1, 96, 3) == 1
-    assert lib.ako_b200_rmsnorm_set_launch(3, 128, 4) == 1
-    assert lib.ako_b200_rmsnorm_set_launch(2, 1024, 8) == 1
+def test_launch_override_validation(mlib) -> None:
+    assert mlib.ako_b200_rmsnorm_set_launch(1, 128, 4) == 0
+    assert mlib.ako_b200_rmsnorm_set_launch(4, 128, 4) == 0
+    assert mlib.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
+    assert mlib.ako_b200_rmsnorm_set_launch(1, 96, 3) == 1
+    assert mlib.ako_b200_rmsnorm_set_launch(3, 128, 4) == 1
+    assert mlib.ako_b200_rmsnorm_set_launch(2, 1024, 8) == 1
 
 
 @pytest.mark.parametrize(
@@ -129,16 +168,36 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path) -> None:
         _native.lib()
 
 
-def test_pdl_switch_returns_previous_setting(lib) -> None:
-    assert lib.ako_b200_set_pdl(0) == 1  # on by default
-    assert lib.ako_b200_set_pdl(5) == 0
-    assert lib.ako_b200_set_pdl(1) == 1
+def test_measurement_block_routes_only_its_own_thread(lib, mlib) -> None:
+    """Inside ``measurement()`` this thread's wrappers call the measurement
+    build; other threads, and this one afterwards, call the product library."""
+    import threading
+
+    seen = {}
+    assert _native.active() is lib
+    with _native.measurement() as m:
+        assert m is mlib and _native.active() is mlib
+        t = threading.Thread(target=lambda: seen.setdefault("other", _native.active()))
+        t.start()
+        t.join()
+    assert seen["other"] is lib and _native.active() is lib
 
 
-def test_rope_launch_override_validation(lib) -> None:
-    assert lib.ako_b200_rope_set_launch(2) == 0
-    assert lib.ako_b200_rope_set_launch(0) == 0
-    assert lib.ako_b200_rope_set_launch(3) == 1
+def test_pdl_switch_returns_previous_setting(mlib) -> None:
+    assert mlib.ako_b200_set_pdl(0) == 1  # on by default
+    assert mlib.ako_b200_set_pdl(5) == 0
+    assert mlib.ako_b200_set_pdl(1) == 1
+
+
+def test_wait_limit_switch_returns_previous_setting(mlib) -> None:
+    assert mlib.ako_b200_measure_set_wait_polls(0) == 1 << 24
+    assert mlib.ako_b200_measure_set_wait_polls(1 << 24) == 0
+
+
+def test_rope_launch_override_validation(mlib) -> None:
+    assert mlib.ako_b200_rope_set_launch(2) == 0
+    assert mlib.ako_b200_rope_set_launch(0) == 0
+    assert mlib.ako_b200_rope_set_launch(3) == 1
 
 
 def _fastdiv(d: int) -> tuple[int, int]:
@@ -166,14 +225,14 @@ def test_multiply_high_division_is_exact(d: int) -> None:
             assert ((((n * m) >> 32) + n) >> l) == n // d, (n, d)
 
 
-def test_staging_hook_validation(lib) -> None:
-    assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(4, 0, 0) == 1
-    assert lib.ako_b200_rmsnorm_set_staging(2, 9, 1) == 1
-    assert lib.ako_b200_take_device_status(None) == 1
+def test_staging_hook_validation(mlib) -> None:
+    assert mlib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
+    assert mlib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
+    assert mlib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
+    assert mlib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
+    assert mlib.ako_b200_rmsnorm_set_staging(4, 0, 0) == 1
+    assert mlib.ako_b200_rmsnorm_set_staging(2, 9, 1) == 1
+    assert mlib.ako_b200_take_device_status(None) == 1
 
 
 def test_host_pipeline_chunking_and_argument_checks() -> None:
@@ -194,3 +253,30 @@ def test_host_pipeline_chunking_and_argument_checks() -> None:
         host.rmsnorm_residual_host(x.to(torch.int32), x.to(torch.int32), torch.ones(8))
     with pytest.raises(ValueError, match="weight must live on the target CUDA device"):
         host.rmsnorm_residual_host(x, x, torch.ones(8))
+
+
+def test_host_slot_capacity_is_bounded() -> None:
+    """Calls of many row counts share few slot sizes: the chunk, or the next
+    power of two at or above a smaller call's rows."""
+    from ako_b200 import host
+
+    caps = {host.slot_capacity(rows, 1024) for rows in range(1, 5000)}
+    assert caps == {1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024}
+    assert host.slot_capacity(1000, 1024) == 1024 and host.slot_capacity(5, 4) == 4
+    assert host.MAX_SLOT_SETS == 4
+
+
+def test_host_pipeline_checks_weight_and_outputs() -> None:
+    from ako_b200 import host
+
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    meta_w = torch.ones(16, device="meta")[::2]  # a strided (8,) view: accepted as a copy, never as-is
+    assert host._host_weight(meta_w, 8, "f").stride(0) == 1
+    with pytest.raises(ValueError, match="Expected weight of shape"):
+        host._host_weight(torch.ones(9), 8, "f")
+    with pytest.raises(ValueError, match="hidden_dim <= 65536"):
+        host._host_weight(torch.ones(65537), 65537, "f")
+    dev_w = torch.ones(8, device="meta")
+    for bad in (torch.zeros(4, 9, dtype=torch.bfloat16), torch.zeros(4, 8, dtype=torch.float32)):
+        with pytest.raises(ValueError, match="y_out must be a host tensor"):
+            host.rmsnorm_residual_host(x, x, dev_w, device="meta", y_out=bad)

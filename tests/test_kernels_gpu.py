@@ -16,7 +16,7 @@ import torch
 
 import golden_data as gd
 from ako_b200 import _native, kernels
-from helpers import TORCH_DTYPE, assert_parity, normal, to_numpy, to_torch
+from helpers import TORCH_DTYPE, assert_parity, check_rmsnorm, normal, to_numpy, to_torch
 from oracle import ako_oracle as O
 from oracle import c_oracle as C
 
@@ -65,13 +65,11 @@ def test_rmsnorm_widths(cuda_device, dtype: str, h: int) -> None:
     r = normal(rng, (rows, h), 0, 1, dtype)
     w = normal(rng, (h,), 1, 0.1, dtype)
     y = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-6)
-    assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y), dtype, "rmsnorm", f"rmsnorm h={h}")
+    check_rmsnorm(x, None, w, 1e-6, dtype, to_numpy(y), what=f"rmsnorm h={h}")
     y, ro = kernels.rmsnorm_residual_cuda_sm100(
         to_torch(x, dtype, cuda_device), to_torch(r, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-5
     )
-    y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
-    np.testing.assert_array_equal(to_numpy(ro), ro_ref)
-    assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"residual h={h}")
+    check_rmsnorm(x, r, w, 1e-5, dtype, to_numpy(y), to_numpy(ro), what=f"residual h={h}")
 
 
 @pytest.mark.parametrize("rows", [1, 3, 4, 5, 127, 1000])
@@ -83,9 +81,7 @@ def test_rmsnorm_row_counts(cuda_device, rows: int) -> None:
         r = normal(rng, (rows, h), 0, 1, O.BF16)
         w = normal(rng, (h,), 1, 0.1, O.BF16)
         y, ro = kernels.rmsnorm_residual_cuda_sm100(*(to_torch(a, O.BF16, cuda_device) for a in (x, r, w)), 1e-5)
-        y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, O.BF16)
-        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
-        assert_parity(y_ref, to_numpy(y), O.BF16, "rmsnorm_residual", f"rows={rows} h={h}")
+        check_rmsnorm(x, r, w, 1e-5, O.BF16, to_numpy(y), to_numpy(ro), what=f"rows={rows} h={h}")
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -161,9 +157,11 @@ def test_rmsnorm_fp32_weight(cuda_device, dtype: str) -> None:
 
 
 def test_every_rmsnorm_launch_shape(cuda_device) -> None:
-    """All built (cluster, threads per row slice, vectors per thread) shapes
-    agree with the oracle, on rows one vector per CTA slice short of full."""
-    lib = _native.lib()
+    """All built (cluster, threads per row slice, vectors per thread) shapes,
+    forced through the measurement build, give the fixed summation order's
+    bits (so every shape gives the same bits), on rows one vector per CTA
+    slice short of full and, for clusters, on rows of whole 32-vector groups
+    per slice."""
     rng = np.random.default_rng(5)
     single = [(32, 1), (32, 2), (32, 4), (32, 8), (64, 2), (64, 4), (64, 8), (128, 1), (128, 2), (128, 4),
               (128, 8), (256, 1), (256, 2), (256, 4), (256, 8), (512, 1), (512, 2), (512, 4), (512, 8),
@@ -172,33 +170,37 @@ def test_every_rmsnorm_launch_shape(cuda_device) -> None:
               (768, 2), (768, 4), (896, 2), (896, 4)]
     split = [(64, 4), (128, 2), (128, 4), (256, 2), (256, 4), (512, 2), (512, 4), (1024, 1), (1024, 2)]
     shapes = [(1, t, n) for t, n in single] + [(c, t, n) for c in (2, 4, 8) for t, n in split]
-    try:
-        for dtype in (O.BF16, O.F32):
-            vec = 8 if dtype == O.BF16 else 4
-            for cl, tpr, nv in shapes:
-                h = cl * (tpr * nv * vec - vec)  # each CTA slice one vector short: exercises the mask
-                if h < vec or h > 65536:
-                    continue
-                rows = 9 if h <= 16384 else 3
-                x = normal(rng, (rows, h), 0, 1, dtype)
-                r = normal(rng, (rows, h), 0, 1, dtype)
-                w = normal(rng, (h,), 1, 0.1, dtype)
-                assert lib.ako_b200_rmsnorm_set_launch(cl, tpr, nv) == 0
-                y, ro = kernels.rmsnorm_residual_cuda_sm100(*(to_torch(a, dtype, cuda_device) for a in (x, r, w)), 1e-5)
-                y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
-                np.testing.assert_array_equal(to_numpy(ro), ro_ref)
-                assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"shape {cl}x{tpr}x{nv} h={h}")
-                y1 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device), 1e-6)
-                assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1), dtype, "rmsnorm", f"shape {cl}x{tpr}x{nv}")
-                if dtype == O.BF16:
-                    # a weight of another dtype takes the kernel's second weight path
-                    w32 = normal(rng, (h,), 1, 0.1, O.F32)
-                    y2 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w32, O.F32, cuda_device),
+    with _native.measurement() as lib:
+        try:
+            for dtype in (O.BF16, O.F32):
+                vec = 8 if dtype == O.BF16 else 4
+                for cl, tpr, nv in shapes:
+                    # one vector short per CTA slice exercises the mask; a cluster
+                    # splits rows only into whole 32-vector groups per slice
+                    nvec = tpr * nv - 1 if cl == 1 else (tpr * nv - 32 if tpr * nv > 32 else 32)
+                    h = cl * nvec * vec
+                    if h < vec or h > 65536:
+                        continue
+                    rows = 9 if h <= 16384 else 3
+                    x = normal(rng, (rows, h), 0, 1, dtype)
+                    r = normal(rng, (rows, h), 0, 1, dtype)
+                    w = normal(rng, (h,), 1, 0.1, dtype)
+                    assert lib.ako_b200_rmsnorm_set_launch(cl, tpr, nv) == 0
+                    args = (to_torch(a, dtype, cuda_device) for a in (x, r, w))
+                    y, ro = kernels.rmsnorm_residual_cuda_sm100(*args, 1e-5)
+                    check_rmsnorm(x, r, w, 1e-5, dtype, to_numpy(y), to_numpy(ro), what=f"shape {cl}x{tpr}x{nv} h={h}")
+                    y1 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(w, dtype, cuda_device),
                                                     1e-6)
-                    assert_parity(C.rmsnorm(x, w32, 1e-6, dtype, O.F32), to_numpy(y2), dtype, "rmsnorm",
-                                  f"fp32 weight, shape {cl}x{tpr}x{nv}")
-    finally:
-        lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
+                    check_rmsnorm(x, None, w, 1e-6, dtype, to_numpy(y1), what=f"shape {cl}x{tpr}x{nv}")
+                    if dtype == O.BF16:
+                        # a weight of another dtype takes the kernel's second weight path
+                        w32 = normal(rng, (h,), 1, 0.1, O.F32)
+                        y2 = kernels.rmsnorm_cuda_sm100(to_torch(x, dtype, cuda_device),
+                                                        to_torch(w32, O.F32, cuda_device), 1e-6)
+                        check_rmsnorm(x, None, w32, 1e-6, dtype, to_numpy(y2), w_dtype=O.F32,
+                                      what=f"fp32 weight, shape {cl}x{tpr}x{nv}")
+        finally:
+            lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -215,24 +217,25 @@ def test_rmsnorm_fitted_thread_counts(cuda_device, dtype: str) -> None:
         w = normal(rng, (h,), 1, 0.1, dtype)
         xt, rt, wt = (to_torch(a, dtype, cuda_device) for a in (x, r, w))
         y, ro = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
-        y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
-        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
-        assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"fitted h={h}")
+        check_rmsnorm(x, r, w, 1e-5, dtype, to_numpy(y), to_numpy(ro), what=f"fitted h={h}")
         y1 = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
-        assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1), dtype, "rmsnorm", f"fitted h={h}")
+        check_rmsnorm(x, None, w, 1e-6, dtype, to_numpy(y1), what=f"fitted h={h}")
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_staged_rmsnorm_matches_oracle(cuda_device, dtype: str) -> None:
-    """The persistent bulk-copy kernel: every stage count and CTA density,
-    rows fewer than CTAs, many rows per CTA, strided rows, fp32 weights. The
-    rounded residual equals the row-resident kernel's bit for bit; the norm
-    is within the parity gates of the oracle (its sum of squares is split
-    over 256 threads, so it can be associated differently from a
-    row-resident launch); no bounded wait ran out."""
-    lib = _native.lib()
+    """The persistent bulk-copy kernel (forced through the measurement
+    build): every stage count and CTA density, rows fewer than CTAs, many rows
+    per CTA, strided rows, fp32 weights. Both outputs equal the row-resident
+    kernel's and the fixed-order model's bit for bit; no bounded wait ran
+    out."""
     rng = np.random.default_rng(31)
     vec = 8 if dtype != O.F32 else 4
+    with _native.measurement() as lib:
+        _staged_cases(lib, cuda_device, rng, dtype, vec)
+
+
+def _staged_cases(lib, cuda_device, rng, dtype, vec) -> None:
     try:
         for h in (vec, 256, 1000 if dtype == O.F32 else 1000 - 1000 % vec, 2048, 4096, 8192, 16384):
             if h % vec or h * (4 if dtype == O.F32 else 2) > 32768:
@@ -250,25 +253,100 @@ def test_staged_rmsnorm_matches_oracle(cuda_device, dtype: str) -> None:
                 assert lib.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
                 y_r, ro_r = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
                 y1_r = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
-                assert torch.equal(ro_s, ro_r), (h, rows)
-                y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
-                np.testing.assert_array_equal(to_numpy(ro_s), ro_ref)
-                assert_parity(y_ref, to_numpy(y_s), dtype, "rmsnorm_residual", f"staged h={h} rows={rows}")
-                assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y1_s), dtype, "rmsnorm", f"staged h={h}")
-                if dtype != O.F32:  # 16-bit outputs: the fp32 association difference never reaches them
-                    assert (y_s.float() - y_r.float()).abs().max().item() <= 2 * 2.0**-7 * y_r.float().abs().max().item()
+                assert torch.equal(ro_s, ro_r) and torch.equal(y_s, y_r) and torch.equal(y1_s, y1_r), (h, rows)
+                check_rmsnorm(x, r, w, 1e-5, dtype, to_numpy(y_s), to_numpy(ro_s), what=f"staged h={h} rows={rows}")
+                check_rmsnorm(x, None, w, 1e-6, dtype, to_numpy(y1_s), what=f"staged h={h}")
         # strided rows and an fp32 weight through the staged path
         base = to_torch(normal(rng, (64, 4096 + 64), 0, 1, dtype), dtype, cuda_device)
         xs = base[:, 64:]
         wf = to_torch(normal(rng, (4096,), 1, 0.1, O.F32), O.F32, cuda_device)
         assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
         y = kernels.rmsnorm_cuda_sm100(xs, wf, 1e-6)
-        assert_parity(C.rmsnorm(to_numpy(xs), to_numpy(wf), 1e-6, dtype, O.F32), to_numpy(y), dtype, "rmsnorm",
-                      "staged strided")
+        check_rmsnorm(to_numpy(xs), None, to_numpy(wf), 1e-6, dtype, to_numpy(y), w_dtype=O.F32,
+                      what="staged strided")
         torch.cuda.synchronize()
         assert _native.take_device_status() == 0
     finally:
         lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+
+
+BATCH_WIDTHS = [(O.BF16, h) for h in (2048, 4096, 5120, 8192, 11008, 14336, 16384, 32768, 65536)] + [
+    (O.F16, 65536), (O.F16, 4096), (O.F32, 4096), (O.F32, 16384), (O.F32, 32768)]
+
+
+@pytest.mark.parametrize("dtype, h", BATCH_WIDTHS, ids=[f"{d}-{h}" for d, h in BATCH_WIDTHS])
+def test_rmsnorm_bits_do_not_depend_on_batch_size(cuda_device, dtype: str, h: int) -> None:
+    """The same rows normalized in batches of 1 to 8192 rows, which the
+    built-in choice runs on different kernels and launch shapes (clusters for
+    decode, latency shapes, the throughput table, the staged and chunked
+    persistent kernels), give identical bits, plain and fused; and they equal
+    the fixed-order model."""
+    tdt = TORCH_DTYPE[dtype]
+    g = torch.Generator(device=cuda_device).manual_seed(h)
+    full = max(1, min(8192, (1 << 27) // h))
+    x = torch.randn(full, h, generator=g, device=cuda_device).to(tdt)
+    r = torch.randn(full, h, generator=g, device=cuda_device).to(tdt)
+    w = (torch.randn(h, generator=g, device=cuda_device) * 0.1 + 1).to(tdt)
+    y_full = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+    yr_full, ro_full = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+    for n in (1, 2, 8, 9, 32, 33, 64, 65, 148, 512, 513, 1024, 2048, 4096):
+        if n >= full:
+            continue
+        assert torch.equal(kernels.rmsnorm_cuda_sm100(x[:n], w, 1e-6), y_full[:n]), (dtype, h, n)
+        yr, ro = kernels.rmsnorm_residual_cuda_sm100(x[:n], r[:n], w, 1e-5)
+        assert torch.equal(yr, yr_full[:n]) and torch.equal(ro, ro_full[:n]), (dtype, h, n)
+    sel = [0, full // 2, full - 1]
+    xs, rs, wn = to_numpy(x[sel]), to_numpy(r[sel]), to_numpy(w)
+    check_rmsnorm(xs, None, wn, 1e-6, dtype, to_numpy(y_full[sel]), what=f"batch h={h}")
+    check_rmsnorm(xs, rs, wn, 1e-5, dtype, to_numpy(yr_full[sel]), to_numpy(ro_full[sel]), what=f"batch h={h}")
+
+
+def test_bounded_wait_expiry_is_reported_and_never_silent(cuda_device) -> None:
+    """A persistent kernel whose bounded wait for a bulk copy runs out fills
+    the rows it could not produce with NaN and records the expiry; every
+    later call of that library is refused until the status is taken. Forced
+    through the measurement build with a wait limit of 0 polls: the waits
+    give up at once while the copies themselves still land, and the kernel
+    drains them before it exits. The product library's status is separate
+    and stays clear."""
+    g = torch.Generator(device=cuda_device).manual_seed(41)
+    bf = torch.bfloat16
+    cases = [(2, 64, 4096, False), (2, 64, 4096, True), (3, 9, 65536, False)]  # staged plain, staged fused, chunked
+    with _native.measurement() as lib:
+        try:
+            for mode, rows, h, fused in cases:
+                x = torch.randn(rows, h, generator=g, device=cuda_device).to(bf)
+                r = torch.randn(rows, h, generator=g, device=cuda_device).to(bf)
+                w = (torch.randn(h, generator=g, device=cuda_device) * 0.1 + 1).to(bf)
+                assert lib.ako_b200_rmsnorm_set_staging(mode, 1 if mode == 2 else 0, 1 if mode == 2 else 0) == 0
+                assert lib.ako_b200_measure_set_wait_polls(0) == 1 << 24
+                if fused:
+                    y, ro = kernels.rmsnorm_residual_cuda_sm100(x, r, w, 1e-5)
+                else:
+                    y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+                lib.ako_b200_measure_set_wait_polls(1 << 24)
+                torch.cuda.synchronize()
+                assert torch.isnan(y.float()).all(), (mode, h)
+                if fused:
+                    assert torch.isnan(ro.float()).all()
+                # every entry point of this library now refuses, before launching
+                with pytest.raises(RuntimeError, match="bounded wait"):
+                    kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+                with pytest.raises(RuntimeError, match="bounded wait"):
+                    kernels.swiglu_cuda_sm100(x, x)
+                assert _native.take_device_status() == 1
+                assert _native.take_device_status() == 0
+                # accepted again, and correct
+                lib.ako_b200_rmsnorm_set_staging(mode, 1 if mode == 2 else 0, 1 if mode == 2 else 0)
+                y = kernels.rmsnorm_cuda_sm100(x, w, 1e-6)
+                check_rmsnorm(to_numpy(x[:3]), None, to_numpy(w), 1e-6, O.BF16, to_numpy(y[:3]), what="after expiry")
+        finally:
+            lib.ako_b200_measure_set_wait_polls(1 << 24)
+            lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+    # the product library never saw an expiry
+    assert _native.take_device_status() == 0
+    x = torch.randn(8, 4096, device=cuda_device).to(bf)
+    assert torch.isfinite(kernels.rmsnorm_cuda_sm100(x, torch.ones(4096, device=cuda_device, dtype=bf)).float()).all()
 
 
 def _kernel_names(fn) -> str:
@@ -326,15 +404,13 @@ def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
         assert (int(m.group(1)) * es, int(m.group(3)), int(m.group(2))) == (access, threads, unroll), (rows, f, got[:300])
 
     # RoPE: rope_vec_kernel<T, NP, INTERLEAVED, HPT>, or the pair-per-thread kernel
-    from ako_b200.dispatch import references as refs
-
     for b, sq, hh, d, style in ((32, 512, 32, 128, "neox"), (8, 1, 8, 128, "neox"), (1, 1, 32, 128, "neox"),
                                 (8, 64, 32, 128, "interleaved"), (8, 64, 8, 98, "neox")):
         out = [ctypes.c_int() for _ in range(5)]
         assert lib.ako_b200_rope_plan(b, sq, hh, d, 0 if style == "neox" else 1, 2, *(ctypes.byref(o) for o in out)) == 0
         access, hpt = out[0].value, out[1].value
         x = torch.randn(b, sq, hh, d, device=cuda_device).to(torch.bfloat16)
-        cos, sin = refs.build_rope_tables(sq, d, device=cuda_device)
+        cos, sin = (to_torch(t, O.F32, cuda_device) for t in O.build_rope_tables(sq, d))
         got = _kernel_names(lambda: kernels.rope_cuda_sm100(x, cos, sin, style))
         if d % 4 == 0:
             m = re.search(r"rope_vec_kernel<[^,]+, (\d+), (?:true|false|1|0), (\d+)>", got)
@@ -353,8 +429,12 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
     chunks). Both keep the row-resident kernel's thread layout (1024 threads
     x 4 or 8 vectors) and sums, so the outputs are bit-identical to it; rows
     are checked against the oracle; uneven rows per CTA, a strided view, and
-    no bounded wait ran out."""
-    lib = _native.lib()
+    no bounded wait ran out. Forced kernels run through the measurement build."""
+    with _native.measurement() as lib:
+        _wide_rows_cases(lib, cuda_device, dtype)
+
+
+def _wide_rows_cases(lib, cuda_device, dtype: str) -> None:
     es = 4 if dtype == O.F32 else 2
     tdt = TORCH_DTYPE[dtype]
     g = torch.Generator(device=cuda_device).manual_seed(7)
@@ -391,11 +471,10 @@ def test_wide_rows_staged_kernel(cuda_device, dtype: str) -> None:
                 assert torch.equal(ro, ro1) and torch.equal(yr, yr1), (dtype, rows, h, mode)
             sel = [0, 1, rows // 2, rows - 1]
             xs, wn = to_numpy(x[sel]), to_numpy(w)
-            assert_parity(C.rmsnorm(xs, wn, 1e-6, dtype), to_numpy(y[sel]), dtype, "rmsnorm", f"wide h={h}")
+            check_rmsnorm(xs, None, wn, 1e-6, dtype, to_numpy(y[sel]), what=f"wide h={h}")
             if fused:
-                y_ref, ro_ref = C.rmsnorm_residual(xs, to_numpy(r[sel]), wn, 1e-5, dtype)
-                np.testing.assert_array_equal(to_numpy(ro[sel]), ro_ref)
-                assert_parity(y_ref, to_numpy(yr[sel]), dtype, "rmsnorm_residual", f"wide h={h}")
+                check_rmsnorm(xs, to_numpy(r[sel]), wn, 1e-5, dtype, to_numpy(yr[sel]), to_numpy(ro[sel]),
+                              what=f"wide h={h}")
         # a strided view through the built-in choice
         assert lib.ako_b200_rmsnorm_set_staging(0, 0, 0) == 0
         base = rand((2048, 32768 + 64))
@@ -543,20 +622,21 @@ def test_rope_bhsd_transposed_view_and_table_slice(cuda_device, dtype: str, styl
 @pytest.mark.parametrize("hpt", [1, 2, 4])
 @pytest.mark.parametrize("style", O.ROPE_STYLES)
 def test_rope_every_heads_per_thread(cuda_device, hpt: int, style: str) -> None:
-    """Each built heads-per-thread variant, head counts not divisible by it."""
-    lib = _native.lib()
+    """Each built heads-per-thread variant (forced through the measurement
+    build), head counts not divisible by it."""
     rng = np.random.default_rng(hpt)
-    try:
-        assert lib.ako_b200_rope_set_launch(hpt) == 0
-        for dtype in DTYPES:
-            for b, s, hh, d in ((2, 7, 1, 128), (1, 3, 3, 64), (3, 5, 40, 128), (1, 9, 32, 128), (2, 2, 5, 16)):
-                x = normal(rng, (b, s, hh, d), 0, 1, dtype)
-                cos, sin = O.build_rope_tables(s, d, offset=11)
-                y = kernels.rope_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(cos, O.F32, cuda_device),
-                                            to_torch(sin, O.F32, cuda_device), style)
-                np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
-    finally:
-        lib.ako_b200_rope_set_launch(0)
+    with _native.measurement() as lib:
+        try:
+            assert lib.ako_b200_rope_set_launch(hpt) == 0
+            for dtype in DTYPES:
+                for b, s, hh, d in ((2, 7, 1, 128), (1, 3, 3, 64), (3, 5, 40, 128), (1, 9, 32, 128), (2, 2, 5, 16)):
+                    x = normal(rng, (b, s, hh, d), 0, 1, dtype)
+                    cos, sin = O.build_rope_tables(s, d, offset=11)
+                    y = kernels.rope_cuda_sm100(to_torch(x, dtype, cuda_device), to_torch(cos, O.F32, cuda_device),
+                                                to_torch(sin, O.F32, cuda_device), style)
+                    np.testing.assert_array_equal(to_numpy(y), O.rope(x, cos, sin, style, dtype))
+        finally:
+            lib.ako_b200_rope_set_launch(0)
 
 
 def test_rope_many_positions(cuda_device) -> None:
@@ -685,8 +765,9 @@ def test_swiglu_extremes(cuda_device) -> None:
 def test_programmatic_launch_changes_no_result(cuda_device) -> None:
     """Every kernel runs with and without programmatic dependent launch; chains
     of dependent calls (each reads the previous call's output) give identical
-    bytes both ways, eagerly and in a CUDA graph."""
-    lib = _native.lib()
+    bytes both ways, eagerly and in a CUDA graph (the switch exists in the
+    measurement build; the product library always launches programmatically
+    and gives the same bytes)."""
     cos, sin = (to_torch(t, O.F32, cuda_device) for t in O.build_rope_tables(96, 128))
     x = torch.randn(96, 4096, device=cuda_device, dtype=torch.bfloat16)
     r = torch.randn_like(x)
@@ -698,27 +779,33 @@ def test_programmatic_launch_changes_no_result(cuda_device) -> None:
         q = kernels.rope_cuda_sm100(y2.view(1, 96, 32, 128), cos[:96], sin[:96], "neox")
         return kernels.swiglu_cuda_sm100(q.view(96, 4096), y)
 
-    try:
-        outs = {}
-        for pdl in (0, 1):
-            lib.ako_b200_set_pdl(pdl)
-            eager = chain()
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                chain()
-            torch.cuda.current_stream().wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                captured = chain()
-            graph.replay()
-            torch.cuda.synchronize()
-            outs[pdl] = (eager.clone(), captured.clone())
-            del graph
-        assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][0], outs[0][1])
-        assert torch.equal(outs[1][0], outs[1][1])
-    finally:
-        lib.ako_b200_set_pdl(1)
+    def run() -> tuple[torch.Tensor, torch.Tensor]:
+        eager = chain()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            chain()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            captured = chain()
+        graph.replay()
+        torch.cuda.synchronize()
+        out = (eager.clone(), captured.clone())
+        del graph
+        return out
+
+    outs = {"product": run()}
+    with _native.measurement() as lib:
+        try:
+            for pdl in (0, 1):
+                lib.ako_b200_set_pdl(pdl)
+                outs[pdl] = run()
+        finally:
+            lib.ako_b200_set_pdl(1)
+    ref = outs[0][0]
+    for eager, captured in outs.values():
+        assert torch.equal(eager, ref) and torch.equal(captured, ref)
 
 
 @pytest.mark.parametrize("dtype", (O.BF16, O.F32))
@@ -891,3 +978,22 @@ def test_randomized_shapes_and_offsets_against_oracle(cuda_device) -> None:
         yq = kernels.rope_cuda_sm100(q, to_torch(cos, O.F32, cuda_device), to_torch(sin, O.F32, cuda_device), style)
         np.testing.assert_array_equal(to_numpy(yq), O.rope(to_numpy(q), cos, sin, style, dtype),
                                       err_msg=f"{what} rope d={d} heads={heads} seq={seq} {style}")
+
+
+def test_host_pipeline_keeps_few_slot_sets(cuda_device) -> None:
+    """Calls of varying row counts reuse power-of-two slot capacities, and at
+    most MAX_SLOT_SETS slot sets stay allocated; every call's outputs equal
+    the device call's."""
+    from ako_b200 import host
+
+    host._slot_cache.clear()
+    w = torch.randn(512, device=cuda_device).to(torch.bfloat16)
+    for rows in (1, 3, 5, 17, 100, 129, 300, 700, 1500, 3000, 33, 6):
+        x = torch.randn(rows, 512).to(torch.bfloat16).pin_memory()
+        r = torch.randn(rows, 512).to(torch.bfloat16).pin_memory()
+        y, ro = host.rmsnorm_residual_host(x, r, w, 1e-5, chunk_rows=1024)
+        torch.cuda.current_stream().synchronize()
+        yd, rod = kernels.rmsnorm_residual_cuda_sm100(x.to(cuda_device), r.to(cuda_device), w, 1e-5)
+        assert torch.equal(y, yd.cpu()) and torch.equal(ro, rod.cpu()), rows
+        assert len(host._slot_cache) <= host.MAX_SLOT_SETS
+    assert {k[1] for k in host._slot_cache} <= {1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024}

@@ -25,21 +25,26 @@ F32, F16, BF16 = 0, 1, 2
 ROWS, STAGED, CHUNKED, GENERIC = 0, 1, 2, 3
 
 
-def plan(rows: int, h: int, dtype: int, residual: bool, aligned: bool = True) -> tuple[int, int, int, int]:
+def plan(rows: int, h: int, dtype: int, residual: bool, aligned: bool = True, lib=None) -> tuple[int, int, int, int]:
+    lib = lib or _native.lib()
     out = [ctypes.c_int() for _ in range(4)]
-    rc = _native.lib().ako_b200_rmsnorm_plan(rows, h, dtype, int(residual), int(aligned), *(ctypes.byref(o) for o in out))
-    assert rc == 0, _native.lib().ako_b200_last_error()
+    rc = lib.ako_b200_rmsnorm_plan(rows, h, dtype, int(residual), int(aligned), *(ctypes.byref(o) for o in out))
+    assert rc == 0, lib.ako_b200_last_error()
     return tuple(o.value for o in out)
 
 
 @pytest.fixture(autouse=True)
 def _built_in_choice():
-    lib = _native.lib()
-    lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
-    lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+    """Overrides live in the measurement build only; reset them around each test."""
+    m = _native.measure_lib()
+    for f in (lambda: m.ako_b200_rmsnorm_set_launch(0, 0, 0), lambda: m.ako_b200_rmsnorm_set_staging(0, 0, 0),
+              lambda: m.ako_b200_swiglu_set_launch(0, 0), lambda: m.ako_b200_rope_set_launch(0)):
+        f()
     yield
-    lib.ako_b200_rmsnorm_set_launch(0, 0, 0)
-    lib.ako_b200_rmsnorm_set_staging(0, 0, 0)
+    m.ako_b200_rmsnorm_set_launch(0, 0, 0)
+    m.ako_b200_rmsnorm_set_staging(0, 0, 0)
+    m.ako_b200_swiglu_set_launch(0, 0)
+    m.ako_b200_rope_set_launch(0)
 
 
 @pytest.mark.parametrize(
@@ -81,6 +86,8 @@ def _built_in_choice():
 )
 def test_built_in_choice(rows, h, dtype, residual, expected) -> None:
     assert plan(rows, h, dtype, residual) == expected
+    # the measurement build makes the same choice while no override is set
+    assert plan(rows, h, dtype, residual, lib=_native.measure_lib()) == expected
 
 
 def test_unaligned_and_ragged_calls_take_the_any_width_kernel() -> None:
@@ -90,16 +97,22 @@ def test_unaligned_and_ragged_calls_take_the_any_width_kernel() -> None:
 
 
 def test_measurement_overrides_are_followed() -> None:
-    lib = _native.lib()
-    assert lib.ako_b200_rmsnorm_set_launch(2, 512, 4) == 0
-    assert plan(8192, 8192, BF16, True) == (ROWS, 2, 512, 4)
-    assert lib.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
-    assert lib.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
-    assert plan(8192, 4096, BF16, True) == (STAGED, 1, 256, 2)
-    assert lib.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
-    assert plan(8192, 32768, BF16, False) == (ROWS, 1, 1024, 4)
-    assert lib.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
-    assert plan(8192, 24576, BF16, False) == (CHUNKED, 1, 1024, 4)
+    """The measurement build follows its overrides; the product library,
+    which has none, keeps its built-in choice meanwhile."""
+    m = _native.measure_lib()
+    assert m.ako_b200_rmsnorm_set_launch(2, 512, 4) == 0
+    assert plan(8192, 8192, BF16, True, lib=m) == (ROWS, 2, 512, 4)
+    assert plan(8192, 8192, BF16, True) == (ROWS, 1, 512, 2)
+    # a split into slices of partial 32-vector groups is not taken (8200 / 8 / 2 = 512.5 vectors)
+    assert plan(8192, 8200 * 2, BF16, True, lib=m)[1] == 1
+    assert m.ako_b200_rmsnorm_set_launch(0, 0, 0) == 0
+    assert m.ako_b200_rmsnorm_set_staging(2, 4, 2) == 0
+    assert plan(8192, 4096, BF16, True, lib=m) == (STAGED, 1, 256, 2)
+    assert plan(8192, 4096, BF16, True) == (ROWS, 1, 256, 2)
+    assert m.ako_b200_rmsnorm_set_staging(1, 0, 0) == 0
+    assert plan(8192, 32768, BF16, False, lib=m) == (ROWS, 1, 1024, 4)
+    assert m.ako_b200_rmsnorm_set_staging(3, 0, 0) == 0
+    assert plan(8192, 24576, BF16, False, lib=m) == (CHUNKED, 1, 1024, 4)
 
 
 def test_invalid_arguments_are_rejected() -> None:
@@ -110,10 +123,12 @@ def test_invalid_arguments_are_rejected() -> None:
     assert lib.ako_b200_rmsnorm_plan(8, 4096, BF16, 0, 1, None, None, None, None) == 1
 
 
-def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool = True) -> tuple[int, int, int]:
+def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool = True, lib=None
+                ) -> tuple[int, int, int]:
+    lib = lib or _native.lib()
     out = [ctypes.c_int() for _ in range(3)]
-    rc = _native.lib().ako_b200_swiglu_plan(rows, f, dtype, int(aligned), int(dense), *(ctypes.byref(o) for o in out))
-    assert rc == 0, _native.lib().ako_b200_last_error()
+    rc = lib.ako_b200_swiglu_plan(rows, f, dtype, int(aligned), int(dense), *(ctypes.byref(o) for o in out))
+    assert rc == 0, lib.ako_b200_last_error()
     return tuple(o.value for o in out)
 
 
@@ -132,24 +147,22 @@ def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool
     ],
 )
 def test_swiglu_built_in_choice(rows, f, dtype, aligned, dense, expected) -> None:
-    _native.lib().ako_b200_swiglu_set_launch(0, 0)
     assert swiglu_plan(rows, f, dtype, aligned, dense) == expected
 
 
 def test_swiglu_override_is_followed() -> None:
-    lib = _native.lib()
-    try:
-        assert lib.ako_b200_swiglu_set_launch(64, 2) == 0
-        assert swiglu_plan(2048, 11008, BF16) == (16, 64, 2)
-        assert swiglu_plan(1, 5632, BF16) == (16, 64, 2)  # an override also skips the decode-sized path
-    finally:
-        lib.ako_b200_swiglu_set_launch(0, 0)
+    m = _native.measure_lib()
+    assert m.ako_b200_swiglu_set_launch(64, 2) == 0
+    assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2)
+    assert swiglu_plan(1, 5632, BF16, lib=m) == (16, 64, 2)  # an override also skips the decode-sized path
+    assert swiglu_plan(2048, 11008, BF16) == (16, 256, 1)
 
 
-def rope_plan(b: int, s: int, h: int, d: int, style: int, dtype: int) -> tuple[int, int, int, int, int]:
+def rope_plan(b: int, s: int, h: int, d: int, style: int, dtype: int, lib=None) -> tuple[int, int, int, int, int]:
+    lib = lib or _native.lib()
     out = [ctypes.c_int() for _ in range(5)]
-    rc = _native.lib().ako_b200_rope_plan(b, s, h, d, style, dtype, *(ctypes.byref(o) for o in out))
-    assert rc == 0, _native.lib().ako_b200_last_error()
+    rc = lib.ako_b200_rope_plan(b, s, h, d, style, dtype, *(ctypes.byref(o) for o in out))
+    assert rc == 0, lib.ako_b200_last_error()
     return tuple(o.value for o in out)
 
 
@@ -172,17 +185,15 @@ NEOX, INTERLEAVED = 0, 1
     ],
 )
 def test_rope_built_in_choice(shape, style, dtype, expected) -> None:
-    _native.lib().ako_b200_rope_set_launch(0)
     assert rope_plan(*shape, style, dtype) == expected
 
 
 def test_rope_override_and_errors() -> None:
+    m = _native.measure_lib()
+    assert m.ako_b200_rope_set_launch(2) == 0
+    assert rope_plan(32, 4096, 32, 128, NEOX, BF16, lib=m) == (16, 2, 8, 16, 2)
+    assert rope_plan(32, 4096, 32, 128, NEOX, BF16) == (16, 1, 8, 32, 1)
     lib = _native.lib()
-    try:
-        assert lib.ako_b200_rope_set_launch(2) == 0
-        assert rope_plan(32, 4096, 32, 128, NEOX, BF16) == (16, 2, 8, 16, 2)
-    finally:
-        lib.ako_b200_rope_set_launch(0)
     out = [ctypes.c_int() for _ in range(5)]
     assert lib.ako_b200_rope_plan(1, 1, 8, 127, NEOX, BF16, *(ctypes.byref(o) for o in out)) == 1
     assert lib.ako_b200_rope_plan(1, 1, 8, 128, 5, BF16, *(ctypes.byref(o) for o in out)) == 1
@@ -206,6 +217,9 @@ def test_every_rmsnorm_plan_covers_its_row(dtype: int, residual: bool) -> None:
                 continue
             assert cluster * threads * vectors >= nvec, (rows, h, kernel, cluster, threads, vectors)
             assert threads <= 1024 and cluster in (1, 2, 4, 8)
+            # the fixed summation order: whole warps per row slice, slices of whole 32-vector groups
+            assert threads % 32 == 0 and nvec % (32 * cluster) == 0 if cluster > 1 else threads % 32 == 0, (
+                rows, h, cluster, threads)
             if kernel in (STAGED, CHUNKED):
                 assert not residual or kernel == STAGED
                 assert cluster == 1

@@ -119,3 +119,86 @@ def test_ulp_distance_counts_steps() -> None:
     b[0] += 2
     b[1] += 1  # more negative by one step
     np.testing.assert_array_equal(O.ulp_distance(a, b, O.BF16), [2, 1, 0])
+
+
+# ---------------------------------------------------- the kernels' sum order
+def _fixed_order_sum_py(sq: np.ndarray, vec: int) -> np.float32:
+    """The CUDA RMSNorm kernels' summation order, restated with fp32 scalars:
+    each vector's squares pairwise (1, 2, 4 apart), each group of 32
+    vectors by a fold (16, 8, 4, 2, 1 apart), then the groups by the same
+    fold, zero-padded to a power of two."""
+    f = np.float32
+    nvec = sq.size // vec
+    vsum = []
+    for v in range(nvec):
+        e = [f(t) for t in sq[v * vec:(v + 1) * vec]]
+        st = 1
+        while st < vec:
+            for i in range(0, vec - st, 2 * st):
+                e[i] = f(e[i] + e[i + st])
+            st *= 2
+        vsum.append(e[0])
+
+    def fold(vals: list) -> np.float32:
+        n = 1
+        while n < len(vals):
+            n *= 2
+        vals = vals + [f(0)] * (n - len(vals))
+        off = n // 2
+        while off >= 1:
+            for i in range(off):
+                vals[i] = f(vals[i] + vals[i + off])
+            off //= 2
+        return vals[0]
+
+    groups = [fold(vsum[g:g + 32] + [f(0)] * (32 - len(vsum[g:g + 32]))) for g in range(0, nvec, 32)]
+    return fold(groups)
+
+
+@pytest.mark.parametrize("dtype", (O.F32, O.F16, O.BF16))
+@pytest.mark.parametrize("h", (8, 64, 256, 264, 1000, 2048, 5128))
+def test_fixed_order_model_follows_its_definition(dtype: str, h: int) -> None:
+    """The C model of the kernels' summation order (the reference the GPU tests
+    hold the kernels to, bit for bit) equals a plain restatement of the
+    documented order, and stays within the reference gate of the
+    reference-order oracle."""
+    vec = 4 if dtype == O.F32 else 8
+    if h % vec:
+        pytest.skip("not whole 16-byte vectors")
+    rng = np.random.default_rng(h)
+    x = O.encode(rng.standard_normal((3, h), dtype=np.float32), dtype)
+    w = O.encode(rng.standard_normal(h, dtype=np.float32) * np.float32(0.1) + 1, dtype)
+    y = C.rmsnorm_fixed_order(x, None, w, 1e-6, dtype)
+    xf, wf = O.decode(x, dtype).astype(np.float32), O.decode(w, dtype).astype(np.float32)
+    for row in range(3):
+        v = xf[row]
+        total = _fixed_order_sum_py((v * v).astype(np.float32), vec)
+        inv = np.float32(1) / np.sqrt(np.float32(total / np.float32(h)) + np.float32(1e-6), dtype=np.float32)
+        expect = O.encode(((v * inv).astype(np.float32) * wf).astype(np.float32), dtype)
+        np.testing.assert_array_equal(y[row], expect)
+    assert int(O.ulp_distance(C.rmsnorm(x, w, 1e-6, dtype), y, dtype).max()) <= (1 if dtype != O.F32 else 4)
+
+
+def test_fixed_order_model_against_reference_golden() -> None:
+    """On the reference's own RMSNorm outputs (golden vectors with rows of
+    whole 16-byte vectors) the fixed order is within 1 ulp for 16-bit
+    outputs and within the fp32 elementwise bound."""
+    from helpers import ULP_F32
+
+    checked = 0
+    for case in gd.cases():
+        if case["op"] not in ("rmsnorm", "rmsnorm_residual"):
+            continue
+        dt = case["dtype"]
+        x = gd.arr(case, "x")
+        h = x.shape[-1]
+        if (h * (4 if dt == O.F32 else 2)) % 16:
+            continue
+        r = gd.arr(case, "r") if case["op"] == "rmsnorm_residual" else None
+        out = C.rmsnorm_fixed_order(x.reshape(-1, h), None if r is None else r.reshape(-1, h),
+                                    gd.arr(case, "w"), case["eps"], dt)
+        y = (out if r is None else out[0]).reshape(gd.arr(case, "y").shape)
+        bound = 1 if dt != O.F32 else ULP_F32[case["op"]]
+        assert int(O.ulp_distance(gd.arr(case, "y"), y, dt).max()) <= bound, case["name"]
+        checked += 1
+    assert checked >= 10
