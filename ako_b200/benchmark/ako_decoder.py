@@ -10,8 +10,9 @@ made from scratch:
 
 * ``torch``: ``backend="torch"``, the reference's eager path;
 * ``ako``: ``backend="ako"``, AKO's selector over its own candidates;
-* ``ako+b200``: the same after :func:`ako_b200.register`, so the sm_100a
-  kernels compete in AKO's validate-then-benchmark selection.
+* ``ako+b200``: the same after ``ako_b200.register(b200_timing=True)``, so
+  the sm_100a kernels compete in AKO's validate-then-benchmark selection,
+  with every candidate timed from a cold B200 L2.
 
 Prefill: batch 8 x 2048 ids into an empty ``KVCache``, logits of the last
 position. Decode: batch 32, 128 greedy steps (argmax fed back) from a
@@ -23,7 +24,7 @@ over the pytorch reference as the selector measured it.
 
     python -m ako_b200.benchmark.ako_decoder [--out FILE] [--modes torch,ako,ako+b200]
 
-Needs the reference package importable (``baseline/_ref`` is put on the path).
+Needs the reference package (``ako_b200.reference``).
 """
 
 from __future__ import annotations
@@ -37,7 +38,6 @@ import sys
 import tempfile
 from pathlib import Path
 
-REF_DIR = Path(__file__).resolve().parents[2] / "baseline" / "_ref"
 MODES = ("torch", "ako", "ako+b200")
 
 
@@ -77,14 +77,16 @@ def _selections(cache_path: Path) -> list[dict]:
 
 def run_mode(mode: str, args) -> dict:
     """One mode in this process (the caller gave it a fresh ``AKO_CACHE_PATH``)."""
-    sys.path.insert(0, str(REF_DIR))
+    from ako_b200.reference import ako
+
+    ako()
     import torch
     from ako.models.decoder import ModelConfig, build_stack
 
     if mode == "ako+b200":
         import ako_b200
 
-        ako_b200.register()
+        ako_b200.register(b200_timing=True)
     dev = torch.device("cuda", 0)
     cfg = ModelConfig(hidden_dim=4096, n_layers=args.layers, n_heads=32, n_kv_heads=8, intermediate_dim=11008,
                       max_seq_len=8192, rope_base=1e4, rope_style="neox", eps=1e-5)
@@ -167,8 +169,9 @@ def main() -> None:
     if args.mode is not None:
         print(json.dumps(run_mode(args.mode, args)))
         return
-    if not (REF_DIR / "ako").is_dir():
-        raise SystemExit(f"the reference package is not installed under {REF_DIR}")
+    from ako_b200.reference import ako
+
+    ako()  # fails here, naming where it looked, when the reference package is missing
     results = []
     child = [f"--{k.replace('_', '-')}={v}" for k, v in vars(args).items() if k not in ("modes", "mode", "out")]
     for mode in args.modes.split(","):

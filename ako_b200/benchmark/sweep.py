@@ -4,13 +4,17 @@ For every op / shape / dtype cell it reports the device time of the sm_100a
 kernel from a cold L2 (differential timing: n x (2x-L2 read, call) minus n
 reads, over n; event steps of ~2 us average out and each call is charged
 the write-back of its outputs), the achieved GB/s on the algorithmic bytes,
-and the fraction of the measured HBM copy bandwidth. Competitors are timed the same way: the unfused reference
-(eager), its ``torch.compile`` form, ``F.rms_norm`` and, when the reference
-package is importable (``--reference-path``), AKO's own Triton kernels. Decode
-cells (one token per sequence) add the wall-clock latency per call of
-back-to-back calls, which is what a decode loop pays, and the device time per
-call of 20 calls captured in one CUDA graph. Each cell is also checked against the eager
-reference with AKO's error budget.
+and the fraction of the measured HBM copy bandwidth. Competitors come from the
+reference package and are timed the same way: AKO's unfused reference
+(eager), its ``torch.compile`` form, ``F.rms_norm`` and AKO's own Triton
+kernels. Ours is timed twice: as shipped (programmatic dependent launch on,
+which lets a call's launch overlap the end of the flush read before it), and
+through the measurement build with programmatic launch off, launched like the
+competitors; the kernel-to-kernel comparison uses the second. Decode cells
+(one token per sequence) add the wall-clock latency per call of back-to-back
+calls, which is what a decode loop pays, and the device time per call of 20
+calls captured in one CUDA graph. Each cell is also checked against AKO's
+eager reference with AKO's error budget.
 
     python -m ako_b200.benchmark.sweep --out sweep.json [--configs 1,2,3,4]
     python -m ako_b200.benchmark.sweep --report sweep.json > sweep.md
@@ -24,29 +28,24 @@ import argparse
 import json
 import math
 import statistics
-import sys
 import time
 from pathlib import Path
 from typing import Any, Callable
 
 import torch
 
-from ako_b200 import kernels
+from ako_b200 import _native, kernels
 from ako_b200.benchmark.timing import Flusher, cold_us
-from ako_b200.dispatch import references as refs
-from ako_b200.dispatch.numerical import error_budget, error_in_ulps, max_abs_error_any
+from ako_b200.reference import ako
 
 DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 
 
-def _reference_package(path: str | None):
-    if path and Path(path).exists() and path not in sys.path:
-        sys.path.insert(0, path)
-    try:
-        from ako.ops import rmsnorm_ref, rmsnorm_torch, rmsnorm_triton, rope_ref, rope_torch, rope_triton, swiglu_ref
-        from ako.ops import swiglu_torch, swiglu_triton
-    except ImportError:
-        return None
+def _reference_package():
+    ako()
+    from ako.ops import rmsnorm_ref, rmsnorm_torch, rmsnorm_triton, rope_ref, rope_torch, rope_triton, swiglu_ref
+    from ako.ops import swiglu_torch, swiglu_triton
+
     return {
         "rmsnorm": {"eager": rmsnorm_ref.rmsnorm_ref, "compile": rmsnorm_torch.rmsnorm_compiled,
                     "triton": rmsnorm_triton.rmsnorm_triton},
@@ -56,15 +55,6 @@ def _reference_package(path: str | None):
         "rope": {"eager": rope_ref.rope_ref, "compile": rope_torch.rope_compiled, "triton": rope_triton.rope_triton},
         "swiglu": {"eager": swiglu_ref.swiglu_ref, "compile": swiglu_torch.swiglu_compiled,
                    "triton": swiglu_triton.swiglu_triton},
-    }
-
-
-def _own_competitors():
-    return {
-        "rmsnorm": {"eager": refs.rmsnorm_ref, "compile": refs.rmsnorm_compiled},
-        "rmsnorm_residual": {"eager": refs.rmsnorm_residual_ref, "compile": refs.rmsnorm_residual_compiled},
-        "rope": {"eager": refs.rope_ref, "compile": refs.rope_compiled},
-        "swiglu": {"eager": refs.swiglu_ref, "compile": refs.swiglu_compiled},
     }
 
 
@@ -205,7 +195,9 @@ def _fmt(v: float | None, nd: int = 3) -> str:
 
 
 def _ratio(c: dict[str, Any], name: str, key: str = "us") -> float | None:
-    theirs, ours = c.get(f"{name}_{key}"), c.get(f"ours_{key}")
+    """Competitor time over ours; device times compare with ours launched like them (no PDL)."""
+    theirs = c.get(f"{name}_{key}")
+    ours = c.get("ours_nopdl_us", c.get("ours_us")) if key == "us" else c.get(f"ours_{key}")
     return theirs / ours if theirs and ours else None
 
 
@@ -230,10 +222,10 @@ def report(summary: dict[str, Any]) -> str:
            "  - `triton`: AKO's own Triton kernels, JIT-compiled for sm_100 on this GPU;",
            "  - `compile`: AKO's `torch.compile` form of the reference;",
            "  - `eager`: AKO's unfused reference.",
-           "  All three come from the reference package installed offline into `baseline/_ref`."
-           if summary.get("reference_package") else
-           "  The reference package was not importable: `compile` and `eager` are this package's restatements.",
-           "- `x` columns: competitor time over ours (above 1: ours is faster).",
+           "  All three come from the reference package (installed offline into `baseline/_ref`).",
+           "- `us nopdl`: ours through the measurement build with programmatic dependent launch off, launched",
+           "  like the competitors. `x` columns and the summary compare each competitor with it (above 1: ours",
+           "  is faster); `us` is ours as shipped (programmatic launch on).",
            "- `ulps`: AKO's `error_in_ulps` of our output against its eager reference.", ""]
     fails = [c for c in cells if not c["parity"]]
     out.append(f"All {len(cells)} cells pass AKO's error budget." if not fails else
@@ -262,14 +254,15 @@ def report(summary: dict[str, Any]) -> str:
     out.append("")
     for cfg in sorted({c["config"] for c in cells}):
         out += [f"## {TITLES[cfg]}", "",
-                "| dtype | cell | us | GB/s | frac | " + " | ".join(f"x {n}" for n in COMPETITORS) + " | ulps |",
-                "|---|---|---:|---:|---:|" + "---:|" * len(COMPETITORS) + "---:|"]
+                "| dtype | cell | us | us nopdl | GB/s | frac | " + " | ".join(f"x {n}" for n in COMPETITORS)
+                + " | ulps |",
+                "|---|---|---:|---:|---:|---:|" + "---:|" * len(COMPETITORS) + "---:|"]
         for c in cells:
             if c["config"] != cfg:
                 continue
             xs = " | ".join(f"{r:.2f}" if (r := _ratio(c, n)) else "-" for n in COMPETITORS)
-            out.append(f"| {c['dtype']} | {cell_label(c)} | {_fmt(c['ours_us'])} | {c['ours_gbs']:.0f} | "
-                       f"{c['frac']:.3f} | {xs} | {c['ulps']:g} |")
+            out.append(f"| {c['dtype']} | {cell_label(c)} | {_fmt(c['ours_us'])} | {_fmt(c.get('ours_nopdl_us'))} | "
+                       f"{c['ours_gbs']:.0f} | {c['frac']:.3f} | {xs} | {c['ulps']:g} |")
         out.append("")
     dec = [c for c in cells if c.get("decode")]
     if dec:
@@ -302,7 +295,6 @@ def main() -> None:
     ap.add_argument("--report", default=None, help="render this sweep JSON as markdown and exit")
     ap.add_argument("--configs", default="1,2,3,4")
     ap.add_argument("--competitors", default="eager,compile,triton,native")
-    ap.add_argument("--reference-path", default="baseline/_ref")
     ap.add_argument("--launches", type=int, default=20, help="calls per timed block")
     ap.add_argument("--blocks", type=int, default=7, help="timed blocks per cell (median)")
     ap.add_argument("--peak-gbs", type=float, default=None)
@@ -320,11 +312,14 @@ def main() -> None:
             peak = float(json.loads(Path("MEASURED_PEAKS.json").read_text())["hbm_gbs"])
         except (OSError, KeyError, ValueError):
             peak = 6650.0
-    ref_pkg = _reference_package(args.reference_path)
-    comps = ref_pkg or _own_competitors()
+    comps = _reference_package()
+    from ako.ops.rmsnorm_torch import rmsnorm_torch_native
+    from ako.ops.rope_ref import build_rope_tables
+    from ako.validation.numerical import error_budget, error_in_ulps, max_abs_error_any
+
     wanted = set(args.competitors.split(","))
     flush = Flusher(dev)
-    tables = {128: refs.build_rope_tables(8192, 128, device=dev)}
+    tables = {128: build_rope_tables(8192, 128, device=dev)}
     results = []
     for cell in cells({int(c) for c in args.configs.split(",")}):
         inputs, kw, nbytes = make_inputs(cell, dev, tables)
@@ -341,9 +336,15 @@ def main() -> None:
         row["ours_us"] = round(us, 3)
         row["ours_gbs"] = round(nbytes / us / 1e3, 1)
         row["frac"] = round(nbytes / us / 1e3 / peak, 4)
+        with _native.measurement() as mlib:
+            mlib.ako_b200_set_pdl(0)
+            try:
+                row["ours_nopdl_us"] = round(device_us(ours, inputs, args.launches, flush, args.blocks), 3)
+            finally:
+                mlib.ako_b200_set_pdl(1)
         candidates = {k: v for k, v in comps[op].items() if k in wanted}
         if op == "rmsnorm" and "native" in wanted:
-            candidates["native"] = refs.rmsnorm_torch_native
+            candidates["native"] = rmsnorm_torch_native
         for name, fn in candidates.items():
             try:
                 row[f"{name}_us"] = round(device_us(fn, inputs, args.launches, flush, args.blocks), 3)
@@ -360,7 +361,7 @@ def main() -> None:
         results.append(row)
         print(json.dumps(row), flush=True)
         del inputs, out, ref
-    summary = {"peak_gbs": peak, "reference_package": ref_pkg is not None, "launches": args.launches,
+    summary = {"peak_gbs": peak, "reference_package": True, "launches": args.launches,
                "blocks": args.blocks,
                "gpu": torch.cuda.get_device_name(dev), "cells": results}
     if args.out:

@@ -20,7 +20,7 @@ norm/residual order as the reference; the layout is chosen for B200:
 
 GEMMs and attention are torch's (cuBLAS / SDPA), as config 5 specifies.
 ``backend="torch"`` runs the same stack with the unfused reference math for
-RMSNorm, RoPE and SwiGLU (``ako_b200.dispatch.references``), for comparison.
+RMSNorm, RoPE and SwiGLU (AKO's own ``ako.ops.*_ref``), for comparison.
 """
 
 from __future__ import annotations
@@ -33,7 +33,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ako_b200 import _native, kernels
-from ako_b200.dispatch import references as refs
+from ako_b200.reference import ops as reference_ops
 
 Backend = Literal["b200", "torch"]
 
@@ -110,8 +110,8 @@ class DecoderLayer(nn.Module):
                 return kernels.rmsnorm_cuda_sm100(x, weight, eps), x
             return kernels.rmsnorm_residual_cuda_sm100(x, residual, weight, eps)
         if residual is None:
-            return refs.rmsnorm_ref(x, weight, eps), x
-        return refs.rmsnorm_residual_ref(x, residual, weight, eps)
+            return reference_ops().rmsnorm_ref(x, weight, eps), x
+        return reference_ops().rmsnorm_residual_ref(x, residual, weight, eps)
 
     def _rope(self, q, k, cos, sin, k_dest):
         style = self.cfg.rope_style
@@ -121,7 +121,7 @@ class DecoderLayer(nn.Module):
             q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
             rope_qk_into(q, k, cos, sin, style, q_out, k_dest)
             return q_out, k_dest
-        q_out, k_out = refs.rope_ref(q, cos, sin, style), refs.rope_ref(k, cos, sin, style)
+        q_out, k_out = reference_ops().rope_ref(q, cos, sin, style), reference_ops().rope_ref(k, cos, sin, style)
         if k_dest is not None:
             k_dest.copy_(k_out)
             k_out = k_dest
@@ -132,7 +132,7 @@ class DecoderLayer(nn.Module):
         gate, up = gu[..., :f], gu[..., f:]
         if self.backend == "b200":
             return kernels.swiglu_cuda_sm100(gate, up)
-        return refs.swiglu_ref(gate, up)
+        return reference_ops().swiglu_ref(gate, up)
 
     # --------------------------------------------------------------- block
     def forward(self, x, residual, cos, sin, cache: KVCache | None, layer: int):
@@ -206,7 +206,7 @@ class Decoder(nn.Module):
     def rope_tables(self, device) -> tuple[torch.Tensor, torch.Tensor]:
         """fp32 tables for positions ``[0, max_seq_len)``, built once, sliced per call."""
         if self._tables is None or self._tables[0].device != torch.device(device):
-            self._tables = refs.build_rope_tables(self.cfg.max_seq_len, self.cfg.head_dim,
+            self._tables = reference_ops().build_rope_tables(self.cfg.max_seq_len, self.cfg.head_dim,
                                                   base=self.cfg.rope_base, device=device)
         return self._tables
 
@@ -229,7 +229,7 @@ class Decoder(nn.Module):
         if self.backend == "b200":
             out, _ = kernels.rmsnorm_residual_cuda_sm100(x, residual, self.final_norm_weight, self.cfg.eps)
         else:
-            out, _ = refs.rmsnorm_residual_ref(x, residual, self.final_norm_weight, self.cfg.eps)
+            out, _ = reference_ops().rmsnorm_residual_ref(x, residual, self.final_norm_weight, self.cfg.eps)
         return out
 
     def forward(self, ids: torch.Tensor, cache: KVCache | None = None) -> torch.Tensor:
@@ -274,7 +274,7 @@ class GraphDecoder:
         if m.backend == "b200":
             h, _ = kernels.rmsnorm_residual_cuda_sm100(x, residual, m.final_norm_weight, m.cfg.eps)
         else:
-            h, _ = refs.rmsnorm_residual_ref(x, residual, m.final_norm_weight, m.cfg.eps)
+            h, _ = reference_ops().rmsnorm_residual_ref(x, residual, m.final_norm_weight, m.cfg.eps)
         nxt = m.lm_head(h[:, -1]).argmax(-1, keepdim=True)
         self.tok.copy_(nxt)
         self.tokens.index_copy_(1, self.step_idx, nxt)
@@ -330,22 +330,39 @@ def build_decoder(cfg: ModelConfig, *, backend: Backend = "b200", device="cuda",
 
 
 def rope_qk_into(q, k, cos, sin, style, q_out, k_out) -> None:
-    """``rope_qk`` writing into caller-provided views (e.g. a KV-cache slot)."""
+    """``rope_qk`` writing into caller-provided views (e.g. a KV-cache slot).
+
+    The same checks as ``rope_qk_cuda_sm100``, plus the outputs': every one of
+    the four tensors is a CUDA tensor of q's dtype on q's device with a
+    contiguous last axis (the kernel indexes all of them in q's element size),
+    and each output has its input's shape.
+    """
     fn = "rope_qk_into"
-    cos, sin = kernels._rope_tables(cos, sin)
+    if style not in kernels.ROPE_STYLES:
+        raise ValueError(f"Unknown RoPE style '{style}', expected one of {kernels.ROPE_STYLES}")
+    kernels._require_cuda(q, fn)
+    kernels._check_rope_args(q, cos, sin, fn)
+    kernels._check_rope_args(k, cos, sin, fn)
     code = kernels._dtype_code(q, "q", fn)
+    for name, t in (("k", k), ("q_out", q_out), ("k_out", k_out)):
+        if t.dtype != q.dtype or t.device != q.device:
+            raise ValueError(f"{fn}: {name} must match q in dtype and device ({q.dtype} on {q.device})")
     for t in (q, k, q_out, k_out):
-        if t.stride(-1) != 1 or not t.is_cuda:
-            raise ValueError(f"{fn}: CUDA tensors with a contiguous last axis required")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{fn}: tensors with a contiguous last axis required")
     if q_out.shape != q.shape or k_out.shape != k.shape:
         raise ValueError(f"{fn}: output shapes must match the inputs")
+    if k.shape[:2] != q.shape[:2] or k.shape[-1] != q.shape[-1]:
+        raise ValueError(f"{fn}: q {tuple(q.shape)} and k {tuple(k.shape)} must share batch, seq_len, head_dim")
+    cos, sin = kernels._rope_tables(cos, sin)
     b, s, qh, d = q.shape
-    status = _native.lib().ako_b200_rope_qk(
-        q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
-        k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
-        cos.data_ptr(), sin.data_ptr(), cos.stride(0),
-        q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_out.stride(2),
-        k_out.data_ptr(), k_out.stride(0), k_out.stride(1), k_out.stride(2),
-        b, s, qh, k.shape[2], d, kernels._STYLE_CODE[style], code, kernels._stream(q.device),
-    )
+    with kernels._DeviceGuard(q.device):
+        status = _native.active().ako_b200_rope_qk(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+            q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_out.stride(2),
+            k_out.data_ptr(), k_out.stride(0), k_out.stride(1), k_out.stride(2),
+            b, s, qh, k.shape[2], d, kernels._STYLE_CODE[style], code, kernels._stream(q.device),
+        )
     _native.raise_for_status(status, fn)

@@ -84,3 +84,37 @@ def test_graph_decode_matches_eager_decode(cuda_device, backend: str) -> None:
         again = gd.run(ids[:, -1:]).clone()
     assert torch.equal(graph_tokens, eager)
     assert torch.equal(again, eager)
+
+
+@pytest.mark.gpu
+def test_config5_width_layer_against_fp32(cuda_device) -> None:
+    """One layer at configuration 5's widths (d 4096, 32 / 8 heads, FFN 11008,
+    vocab 32000, bf16, N(0, 0.02) weights): prefill of 2 x 64 tokens and 4
+    cached decode steps. Both bf16 stacks are compared with an fp32
+    evaluation of the same weights on the same tokens. The bound: the B200
+    stack's largest logit error is at most 1.5x the reference-math stack's
+    plus 0.01, and their hidden states agree to 5% of their largest magnitude
+    (a few bf16 ulp there) with cosine similarity above 0.9999."""
+    cfg = ModelConfig(n_layers=1, max_seq_len=8192)
+    ids = torch.randint(0, cfg.vocab_size, (2, 68), generator=torch.Generator().manual_seed(4)).to(cuda_device)
+    logits, hidden = {}, {}
+    for backend in ("b200", "torch", "fp32"):
+        m = build_decoder(cfg, backend="torch" if backend == "fp32" else backend, device=cuda_device,
+                          dtype=torch.bfloat16, seed=6)
+        if backend == "fp32":
+            m = m.float()
+        with torch.inference_mode():
+            cache = m.new_cache(2, 72)
+            pre = m.hidden(ids[:, :64], cache)
+            steps = [m.hidden(ids[:, i:i + 1], cache) for i in range(64, 68)]
+            h = torch.cat([pre, *steps], 1).float()
+            hidden[backend] = h
+            logits[backend] = m.lm_head(h.to(m.lm_head.weight.dtype)).float()
+        del m
+        torch.cuda.empty_cache()
+    err = {b: (logits[b] - logits["fp32"]).abs().max().item() for b in ("b200", "torch")}
+    assert err["b200"] <= 1.5 * err["torch"] + 0.01, err
+    d = (hidden["b200"] - hidden["torch"]).abs().max().item()
+    scale = hidden["torch"].abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(hidden["b200"].flatten(), hidden["torch"].flatten(), dim=0).item()
+    assert d <= 0.05 * scale and cos > 0.9999, (d, scale, cos)

@@ -39,7 +39,7 @@ def _worker(rank: int, world: int, port: int, out) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
                       LOCAL_RANK=str(rank))
     from ako_b200 import sharding
-    from ako_b200.dispatch import references as refs
+    from ako_b200.reference import ops
 
     w, r, _ = sharding.init("gloo", timeout_s=60)
     # Each rank normalizes its own block of a global batch, with no data
@@ -48,7 +48,7 @@ def _worker(rank: int, world: int, port: int, out) -> None:
     x = torch.randn(10, 64, generator=g)
     wt = torch.randn(64, generator=g)
     lo, hi = sharding.shard_range(x.shape[0], w, r)
-    local = refs.rmsnorm_ref(x[lo:hi], wt)
+    local = ops().rmsnorm_ref(x[lo:hi], wt)
     sharding.barrier()
     job = sharding.max_over_ranks(1.5 + r)
     out.put((r, lo, hi, local, job))
@@ -68,11 +68,11 @@ def test_two_ranks_over_gloo() -> None:
         assert p.exitcode == 0
     got.sort()
     assert [g[4] for g in got] == [2.5, 2.5]
-    from ako_b200.dispatch import references as refs
+    from ako_b200.reference import ops
 
     g = torch.Generator().manual_seed(0)
     x = torch.randn(10, 64, generator=g)
     wt = torch.randn(64, generator=g)
     whole = torch.cat([g_[3] for g_ in got])
-    assert torch.equal(whole, refs.rmsnorm_ref(x, wt)) or torch.allclose(whole, refs.rmsnorm_ref(x, wt), atol=1e-6)
+    assert torch.equal(whole, ops().rmsnorm_ref(x, wt)) or torch.allclose(whole, ops().rmsnorm_ref(x, wt), atol=1e-6)
     assert got[0][1:3] == (0, 5) and got[1][1:3] == (5, 10)
