@@ -8,17 +8,23 @@ caller holding host data pays one call, and so the benchmark can time the
 whole path a host caller sees.
 
 The kernels are called through the C ABI (``ako_b200_rmsnorm_residual``)
-on device slot buffers allocated once per (device, shape, dtype).
+on device slot buffers. A slot set is allocated once per (device, capacity,
+hidden size, dtype, slot count), where the capacity in rows is the chunk
+size, or for calls with fewer rows the next power of two at or above their
+row count; at most ``MAX_SLOT_SETS`` sets are kept (least recently used
+first out, after its streams have drained), so callers with varying batch
+sizes do not accumulate device memory.
 """
 
 from __future__ import annotations
 
+from collections import OrderedDict
 from dataclasses import dataclass
 
 import torch
 
 from ako_b200 import _native
-from ako_b200.kernels import _DTYPE_CODE
+from ako_b200.kernels import _DTYPE_CODE, MAX_HIDDEN_DIM
 
 # Per operand per chunk. A call's first host-to-device chunk and last
 # device-to-host chunk cannot overlap the other direction, so smaller chunks
@@ -27,6 +33,8 @@ from ako_b200.kernels import _DTYPE_CODE
 # 64 MB, 94.2 for 16 MB and 91.5 for 8 MB (a bidirectional copy of the same
 # bytes: 99.3).
 DEFAULT_CHUNK_BYTES = 32 << 20
+#: Slot sets kept at once (each is 4 operands x slots x capacity rows).
+MAX_SLOT_SETS = 4
 
 
 @dataclass
@@ -43,18 +51,35 @@ class _Slots:
     ev_out: list[torch.cuda.Event]
 
 
-_slot_cache: dict[tuple, _Slots] = {}
+_slot_cache: OrderedDict[tuple, _Slots] = OrderedDict()
 
 
-def _slots(device: torch.device, chunk_rows: int, hidden: int, dtype: torch.dtype, n: int) -> _Slots:
-    key = (device, chunk_rows, hidden, dtype, n)
+def slot_capacity(rows: int, chunk_rows: int) -> int:
+    """Rows a slot holds for a call of ``rows`` rows in chunks of ``chunk_rows``:
+    the chunk, or the next power of two at or above a smaller call's rows."""
+    if rows >= chunk_rows:
+        return chunk_rows
+    cap = 1
+    while cap < rows:
+        cap *= 2
+    return min(cap, chunk_rows)
+
+
+def _slots(device: torch.device, capacity: int, hidden: int, dtype: torch.dtype, n: int) -> _Slots:
+    key = (device, capacity, hidden, dtype, n)
     s = _slot_cache.get(key)
-    if s is None:
-        mk = lambda: [torch.empty(chunk_rows, hidden, dtype=dtype, device=device) for _ in range(n)]  # noqa: E731
-        ev = lambda: [torch.cuda.Event() for _ in range(n)]  # noqa: E731
-        s = _Slots(mk(), mk(), mk(), mk(), torch.cuda.Stream(device), torch.cuda.Stream(device),
-                   torch.cuda.Stream(device), ev(), ev(), ev())
-        _slot_cache[key] = s
+    if s is not None:
+        _slot_cache.move_to_end(key)
+        return s
+    while len(_slot_cache) >= MAX_SLOT_SETS:
+        _, old = _slot_cache.popitem(last=False)
+        for st in (old.s_in, old.s_run, old.s_out):
+            st.synchronize()  # nothing in flight still uses its buffers
+    mk = lambda: [torch.empty(capacity, hidden, dtype=dtype, device=device) for _ in range(n)]  # noqa: E731
+    ev = lambda: [torch.cuda.Event() for _ in range(n)]  # noqa: E731
+    s = _Slots(mk(), mk(), mk(), mk(), torch.cuda.Stream(device), torch.cuda.Stream(device),
+               torch.cuda.Stream(device), ev(), ev(), ev())
+    _slot_cache[key] = s
     return s
 
 
@@ -88,12 +113,14 @@ def rmsnorm_residual_host(
     code = _DTYPE_CODE.get(x.dtype)
     if code is None:
         raise ValueError(f"{fn} supports float32/float16/bfloat16, got {x.dtype}")
+    for name, t in (("y_out", y_out), ("residual_out", residual_out)):
+        if t is not None and (t.shape != x.shape or t.dtype != x.dtype or t.is_cuda):
+            raise ValueError(f"{fn}: {name} must be a host tensor of x's shape {tuple(x.shape)} and dtype {x.dtype}")
     dev = torch.device(device) if device is not None else weight.device
     if dev.type != "cuda" or weight.device != dev:
         raise ValueError(f"{fn}: weight must live on the target CUDA device")
     hidden = x.shape[-1]
-    if weight.shape != (hidden,):
-        raise ValueError(f"Expected weight of shape ({hidden},), got {tuple(weight.shape)}")
+    weight = _host_weight(weight, hidden, fn)
     wcode = _DTYPE_CODE.get(weight.dtype)
     if wcode is None:
         raise ValueError(f"{fn}: unsupported weight dtype {weight.dtype}")
@@ -107,9 +134,10 @@ def rmsnorm_residual_host(
         return y, ro
     if chunk_rows is None:
         chunk_rows = max(1, DEFAULT_CHUNK_BYTES // max(1, hidden * x.element_size()))
+    capacity = slot_capacity(rows, chunk_rows)
     chunk_rows = min(chunk_rows, rows)
-    st = _slots(dev, chunk_rows, hidden, x.dtype, slots)
-    lib = _native.lib()
+    st = _slots(dev, capacity, hidden, x.dtype, slots)
+    lib = _native.active()
     w_ptr = weight.data_ptr()
     with torch.cuda.device(dev):
         caller = torch.cuda.current_stream(dev)
@@ -141,6 +169,16 @@ def rmsnorm_residual_host(
                 st.ev_out[k].record(st.s_out)
         caller.wait_stream(st.s_out)
     return y, ro
+
+
+def _host_weight(weight: torch.Tensor, hidden: int, fn: str) -> torch.Tensor:
+    """The weight as the C ABI takes it: ``(hidden,)`` and contiguous (a strided
+    view is copied, as the device wrappers do)."""
+    if hidden > MAX_HIDDEN_DIM:
+        raise ValueError(f"{fn} supports hidden_dim <= {MAX_HIDDEN_DIM}, got {hidden}")
+    if weight.shape != (hidden,):
+        raise ValueError(f"Expected weight of shape ({hidden},), got {tuple(weight.shape)}")
+    return weight if weight.stride(0) == 1 else weight.contiguous()
 
 
 def launches_per_call(rows: int, hidden: int, element_size: int, chunk_rows: int | None = None) -> int:

@@ -57,6 +57,24 @@ def max_over_ranks(value: float, device: torch.device | None = None) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(value: float, device: torch.device | None = None) -> float:
+    """Sum of ``value`` over all ranks (the bytes of a step over all shards)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return value
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device or "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item()) if not isinstance(value, int) else int(round(t.item()))
+
+
+def all_over_ranks(flag: bool, device: torch.device | None = None) -> bool:
+    """True when ``flag`` holds on every rank (a per-shard check)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return bool(flag)
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=device or "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
 def finish() -> None:
     if dist.is_available() and dist.is_initialized():
         dist.destroy_process_group()

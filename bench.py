@@ -1,40 +1,60 @@
 #!/usr/bin/env python
 """Benchmark of the B200 kernels behind AKO's dispatcher API; prints ONE JSON line.
 
-Metric: achieved HBM GB/s = algorithmic bytes / device time.
+Metric: achieved HBM GB/s = algorithmic bytes / device time (the first half
+of the reference configuration's metric; the decoder's prefill and decode
+tokens per second, the second half, are in ``decoder``).
+
 A step is one pass of the hot path over one batch: by default one fused
 residual-add RMSNorm (``rmsnorm_residual``) over config 2's largest cell,
-32768 rows x 16384 bf16 per GPU (4.3 GB moved per step, far above the 126 MB
-L2, so back-to-back steps need no flush).
+32768 rows x 16384 bf16 (4.3 GB moved, far above the 126 MB L2, so
+back-to-back steps need no flush).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-* ``value``: whole-job GB/s, inputs resident in HBM, CUDA events on the
-  launching stream around exactly K steps, max over ranks.
+Multi-GPU (torchrun, one process per GPU): the step's batch is one global
+batch whose rows are split into contiguous blocks by
+``ako_b200.sharding.shard_range`` (strong scaling; ``--scaling weak`` gives
+every rank a whole batch instead). Every rank generates only its own rows,
+from seeds that depend on the global row index, so the union of the shards is
+the one-GPU batch. No collective touches the data path: only a barrier, the
+max of the per-rank device times and the AND of the per-rank parity checks.
+
+* ``value``: whole-job GB/s = the global batch's bytes / the slowest rank's
+  time, inputs resident in HBM, CUDA events on the launching stream around
+  exactly K steps.
+* ``weak`` (N > 1): the same with a whole batch per rank.
+* ``parity``: rows of every shard against the C model of the kernels' fixed
+  summation order (bit for bit) and the reference-order oracle (the gate).
 * ``e2e``: the same metric through the host-buffer call
   (``ako_b200.host.rmsnorm_residual_host``): pinned host inputs copied in and
   results copied out inside the timed region, every step.
-* ``roofline``: the kernel's achieved bytes per launch / measured HBM copy
-  bandwidth (``MEASURED_PEAKS.json``), with DRAM traffic from the committed
-  ncu summary of this workload.
-* ``cpu_baseline``: the C oracle (a restatement of AKO's unfused reference,
-  all host threads) on a bounded row sample of the same workload, rank 0, N=1.
-* ``ops``: the other ops at their largest benchmark cell (N=1), device time
+* ``roofline``: this rank's kernel bytes per launch / its launch time against
+  the measured HBM copy bandwidth (``MEASURED_PEAKS.json``), with the DRAM
+  traffic of one launch from the committed ncu summary of this workload.
+* ``cpu_baseline``: AKO's own unfused reference (``ako.ops.rmsnorm_ref.
+  rmsnorm_residual_ref``) on CPU tensors, timed with AKO's ``bench_op``, on
+  rows of the same workload, with the CPU described; the C restatement of it
+  (``oracle/``, all host threads) as a second number. Rank 0, N = 1.
+* ``ops``: the other ops at their largest benchmark cells (N = 1), device time
   per call from a cold L2 (differential timing).
+* ``decoder``: configuration 5 (N = 1): prefill and decode tokens per second
+  of the B200 decoder (eager and one CUDA graph per step) next to the same
+  stack on the reference math, and AKO's own decoder stack through AKO's
+  selector with and without the sm_100a candidates.
 
-Multi-GPU (torchrun): every rank owns its own row shard (weak scaling); no
-collective touches the data path, only the max of the timings.
-``--impl reference`` times the CPU oracle port of AKO's reference (rank 0).
+``--impl reference`` times AKO's own reference (``rmsnorm_residual_ref`` on
+CPU tensors, through ``bench_op``) on rank 0 over the workload's rows that the
+host memory holds, and prints the same line with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
 
 import argparse
-import datetime
 import json
 import os
+import platform
 import re
-import statistics
 import sys
 import time
 from pathlib import Path
@@ -44,10 +64,9 @@ sys.path.insert(0, str(REPO))
 
 import torch  # noqa: E402
 
-BF16_BYTES = 2
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e datasheet figure, the metric's "% of ~8 TB/s"
-L2_BYTES = 126 * 1024 * 1024
+ROW_BLOCK = 1024  # rows generated from one seed; shards start on these boundaries when they can
 
 WORKLOADS = {
     # name: (op, dims, dtype)
@@ -56,8 +75,11 @@ WORKLOADS = {
     "rmsnorm_residual_bf16_8192x4096": ("rmsnorm_residual", (8192, 4096), torch.bfloat16),
     "rmsnorm_residual_bf16_4096x8192": ("rmsnorm_residual", (4096, 8192), torch.bfloat16),
     "rmsnorm_fp32_2048x4096": ("rmsnorm", (2048, 4096), torch.float32),
+    "rmsnorm_bf16_8192x65536": ("rmsnorm", (8192, 65536), torch.bfloat16),
+    "rmsnorm_bf16_8192x32768": ("rmsnorm", (8192, 32768), torch.bfloat16),
     "rope_q_bf16_32x4096x32x128": ("rope", (32, 4096, 32, 128), torch.bfloat16),
     "rope_k_bf16_32x4096x8x128": ("rope", (32, 4096, 8, 128), torch.bfloat16),
+    "rope_qk_bf16_32x4096x32+8x128": ("rope_qk", (32, 4096, 32, 128), torch.bfloat16),
     "rope_q_bf16_8x512x32x128": ("rope", (8, 512, 32, 128), torch.bfloat16),
     "swiglu_bf16_16384x14336": ("swiglu", (16384, 14336), torch.bfloat16),
     "swiglu_packed_bf16_16384x14336": ("swiglu_packed", (16384, 14336), torch.bfloat16),
@@ -66,7 +88,9 @@ WORKLOADS = {
     # small cases of the same kernels (a few hundred MB, above L2) for ncu captures
     "rmsnorm_residual_bf16_2048x16384": ("rmsnorm_residual", (2048, 16384), torch.bfloat16),
     "rmsnorm_residual_bf16_4096x4096": ("rmsnorm_residual", (4096, 4096), torch.bfloat16),
+    "rmsnorm_bf16_1024x65536": ("rmsnorm", (1024, 65536), torch.bfloat16),
     "rope_q_bf16_16x512x32x128": ("rope", (16, 512, 32, 128), torch.bfloat16),
+    "rope_qk_bf16_8x512x32+8x128": ("rope_qk", (8, 512, 32, 128), torch.bfloat16),
 }
 DEFAULT_WORKLOAD = "rmsnorm_residual_bf16_32768x16384"
 OPS_EXTRA = [
@@ -74,6 +98,7 @@ OPS_EXTRA = [
     "rmsnorm_residual_bf16_32768x4096",
     "rope_q_bf16_32x4096x32x128",
     "rope_k_bf16_32x4096x8x128",
+    "rope_qk_bf16_32x4096x32+8x128",
     "swiglu_bf16_16384x14336",
     "swiglu_packed_bf16_16384x14336",
 ]
@@ -84,50 +109,97 @@ def log(*a: object) -> None:
 
 
 # ----------------------------------------------------------------- workloads
-class Workload:
-    """Inputs in HBM, one kernel launch per step, and its algorithmic bytes."""
+def row_block(block: int, hidden: int, dtype: torch.dtype, device, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rows ``[block * ROW_BLOCK, (block + 1) * ROW_BLOCK)`` of x and residual
+    of the seeded global batch (N(0, 1)), the same on every rank and GPU count."""
+    g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + block)
+    x = torch.randn(ROW_BLOCK, hidden, generator=g, device=device).to(dtype)
+    r = torch.randn(ROW_BLOCK, hidden, generator=g, device=device).to(dtype)
+    return x, r
 
-    def __init__(self, name: str, device: torch.device, seed: int = 0) -> None:
+
+def global_rows(lo: int, hi: int, hidden: int, dtype: torch.dtype, device, seed: int):
+    """Rows ``[lo, hi)`` of x and residual of the seeded global batch."""
+    x = torch.empty(hi - lo, hidden, dtype=dtype, device=device)
+    r = torch.empty_like(x)
+    for b in range(lo // ROW_BLOCK, (hi + ROW_BLOCK - 1) // ROW_BLOCK):
+        bx, br = row_block(b, hidden, dtype, device, seed)
+        a, z = max(lo, b * ROW_BLOCK), min(hi, (b + 1) * ROW_BLOCK)
+        x[a - lo:z - lo] = bx[a - b * ROW_BLOCK:z - b * ROW_BLOCK]
+        r[a - lo:z - lo] = br[a - b * ROW_BLOCK:z - b * ROW_BLOCK]
+    return x, r
+
+
+def weight(hidden: int, dtype: torch.dtype, device, seed: int) -> torch.Tensor:
+    """The workload's weight, N(1, 0.1), from a seed no row block uses."""
+    g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 1_000_000)
+    return (torch.randn(hidden, generator=g, device=device) * 0.1 + 1.0).to(dtype)
+
+
+class Workload:
+    """Inputs in HBM, one kernel launch per step, and its algorithmic bytes.
+
+    Row ops hold rows ``[lo, hi)`` of the workload's seeded global batch; the
+    other ops hold the whole cell.
+    """
+
+    def __init__(self, name: str, device: torch.device, seed: int = 0, rows: tuple[int, int] | None = None) -> None:
         from ako_b200 import kernels
 
         self.name = name
         self.op, self.dims, self.dtype = WORKLOADS[name]
         b = torch.tensor([], dtype=self.dtype).element_size()
-        g = torch.Generator(device=device).manual_seed(seed)
-        rnd = lambda *s, mean=0.0, std=1.0: (torch.randn(*s, generator=g, device=device) * std + mean).to(self.dtype)  # noqa: E731
+        self.element_size = b
         if self.op in ("rmsnorm", "rmsnorm_residual"):
             m, h = self.dims
-            self.x = rnd(m, h)
-            self.w = rnd(h, mean=1.0, std=0.1)
+            self.lo, self.hi = rows or (0, m)
+            n = self.hi - self.lo
+            self.x, r = global_rows(self.lo, self.hi, h, self.dtype, device, seed)
+            self.w = weight(h, self.dtype, device, seed)
             if self.op == "rmsnorm":
-                self.bytes = 2 * m * h * b + h * b
+                del r
+                self.bytes = 2 * n * h * b + h * b
                 self.fn = lambda: kernels.rmsnorm_cuda_sm100(self.x, self.w, 1e-6)
             else:
-                self.r = rnd(m, h)
-                self.bytes = 4 * m * h * b + h * b
+                self.r = r
+                self.bytes = 4 * n * h * b + h * b
                 self.fn = lambda: kernels.rmsnorm_residual_cuda_sm100(self.x, self.r, self.w, 1e-5)
-            self.desc = {"rows": m, "hidden": h}
-        elif self.op == "rope":
+            self.desc = {"rows": n, "hidden": h}
+            self.kernel = "ako_b200::rms_rows_kernel"
+            return
+        g = torch.Generator(device=device).manual_seed(seed)
+        rnd = lambda *s, mean=0.0, std=1.0: (torch.randn(*s, generator=g, device=device) * std + mean).to(self.dtype)  # noqa: E731
+        if self.op in ("rope", "rope_qk"):
             bb, s, hh, d = self.dims
             from ako_b200.api import build_rope_tables
 
             cos, sin = build_rope_tables(8192, d, device=device)
             self.cos, self.sin = cos[:s], sin[:s]
             self.x = rnd(bb, s, hh, d)
-            self.bytes = 2 * bb * s * hh * d * b + s * (d // 2) * 4 * 2
-            self.fn = lambda: kernels.rope_cuda_sm100(self.x, self.cos, self.sin, "neox")
-            self.desc = {"batch": bb, "seq": s, "heads": hh, "head_dim": d, "style": "neox", "table": "fp32 [8192, 64] sliced"}
-        else:
-            m, f = self.dims
-            if self.op == "swiglu_packed":
-                self.packed = rnd(m, 2 * f, std=2.0)
-                self.g, self.u = self.packed[:, :f], self.packed[:, f:]
+            table = s * (d // 2) * 4 * 2
+            if self.op == "rope":
+                self.bytes = 2 * bb * s * hh * d * b + table
+                self.fn = lambda: kernels.rope_cuda_sm100(self.x, self.cos, self.sin, "neox")
+                self.desc = {"batch": bb, "seq": s, "heads": hh, "head_dim": d, "style": "neox",
+                             "table": "fp32 [8192, 64] sliced"}
             else:
-                self.g, self.u = rnd(m, f, std=2.0), rnd(m, f, std=2.0)
-            self.bytes = 3 * m * f * b
-            self.fn = lambda: kernels.swiglu_cuda_sm100(self.g, self.u)
-            self.desc = {"rows": m, "hidden": f, "packed": self.op == "swiglu_packed"}
-        self.launches_per_step = 1
+                self.k = rnd(bb, s, 8, d)
+                self.bytes = 2 * bb * s * (hh + 8) * d * b + table
+                self.fn = lambda: kernels.rope_qk_cuda_sm100(self.x, self.k, self.cos, self.sin, "neox")
+                self.desc = {"batch": bb, "seq": s, "q_heads": hh, "k_heads": 8, "head_dim": d, "style": "neox",
+                             "table": "fp32 [8192, 64] sliced, read once for q and k"}
+            self.kernel = "ako_b200::rope_vec_kernel"
+            return
+        m, f = self.dims
+        if self.op == "swiglu_packed":
+            self.packed = rnd(m, 2 * f, std=2.0)
+            self.g, self.u = self.packed[:, :f], self.packed[:, f:]
+        else:
+            self.g, self.u = rnd(m, f, std=2.0), rnd(m, f, std=2.0)
+        self.bytes = 3 * m * f * b
+        self.fn = lambda: kernels.swiglu_cuda_sm100(self.g, self.u)
+        self.desc = {"rows": m, "hidden": f, "packed": self.op == "swiglu_packed"}
+        self.kernel = "ako_b200::swiglu_kernel"
 
     def step(self) -> None:
         self.fn()
@@ -147,7 +219,7 @@ def dist_setup() -> tuple[int, int, int]:
         saved = os.dup(1)
         os.dup2(2, 1)
         try:
-            sharding.init("nccl", device=torch.device("cuda", local))
+            sharding.init("nccl", timeout_s=300.0, device=torch.device("cuda", local))
             sharding.barrier()
         finally:
             sys.stdout.flush()
@@ -156,25 +228,16 @@ def dist_setup() -> tuple[int, int, int]:
     return world, rank, local
 
 
-def barrier(world: int) -> None:
-    from ako_b200 import sharding
-
-    sharding.barrier()
-
-
-def max_over_ranks(v: float, world: int, device: torch.device) -> float:
-    from ako_b200 import sharding
-
-    return sharding.max_over_ranks(v, device)
-
-
-def timed_region(step, k: int, w: int, world: int, marks=None) -> float:
-    """W untimed steps, then exactly K steps between events; ms on this rank.
+def timed_region(step, k: int, w: int, marks=None) -> float:
+    """W untimed steps, then exactly K steps between events on the launching
+    stream, with a barrier and a synchronize on both sides; ms on this rank.
     ``marks`` (a clock sampler) gets the host times around the timed steps."""
+    from ako_b200 import sharding
+
     for _ in range(w):
         step()
     torch.cuda.synchronize()
-    barrier(world)
+    sharding.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if marks is not None:
@@ -186,7 +249,7 @@ def timed_region(step, k: int, w: int, world: int, marks=None) -> float:
     torch.cuda.synchronize()
     if marks is not None:
         marks.mark_end()
-    barrier(world)
+    sharding.barrier()
     return start.elapsed_time(end)
 
 
@@ -209,6 +272,122 @@ def ncu_traffic(workload: str) -> int | None:
     return int(m.group(1)) if m else None
 
 
+# ------------------------------------------------------------------ parity
+def shard_parity(wl: Workload) -> dict:
+    """Rows of this rank's shard (its first, middle and last) against the C
+    model of the kernels' fixed summation order (bit for bit) and the
+    reference-order oracle (AKO's gate), on the host."""
+    import numpy as np
+
+    from oracle import ako_oracle as O
+    from oracle import c_oracle as C
+
+    def host(t: torch.Tensor) -> np.ndarray:
+        t = t.detach().cpu().contiguous()
+        return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+    n = wl.hi - wl.lo
+    sel = sorted({0, n // 2, n - 1})
+    dt = {torch.bfloat16: O.BF16, torch.float16: O.F16, torch.float32: O.F32}[wl.dtype]
+    xs, w = host(wl.x[sel]), host(wl.w)
+    ok, worst = True, 0
+    if wl.op == "rmsnorm_residual":
+        rs = host(wl.r[sel])
+        y, ro = (host(t[sel]) for t in wl.fn())
+        ym, rom = C.rmsnorm_fixed_order(xs, rs, w, 1e-5, dt)
+        yo, roo = C.rmsnorm_residual(xs, rs, w, 1e-5, dt)
+        ok = bool(np.array_equal(y, ym) and np.array_equal(ro, rom) and np.array_equal(ro, roo))
+    else:
+        y = host(wl.fn()[sel])
+        ym = C.rmsnorm_fixed_order(xs, None, w, 1e-6, dt)
+        yo = C.rmsnorm(xs, w, 1e-6, dt)
+        ok = bool(np.array_equal(y, ym))
+    worst = int(O.ulp_distance(yo, y, dt).max())
+    ok = ok and worst <= (2 if dt != O.F32 else 6)
+    return {"ok": ok, "rows": [wl.lo + i for i in sel], "max_ulp_vs_reference_order": worst}
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_description() -> dict:
+    model = platform.processor() or ""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+
+
+def host_rows_that_fit(rows: int, hidden: int, element_size: int) -> int:
+    """Rows of the workload AKO's CPU reference can run on in host memory: its
+    inputs, outputs and fp32 temporaries (about 5 fp32 copies of a row) with a
+    2x margin, within half of the memory available now."""
+    try:
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    except (ValueError, OSError):
+        avail = 16 << 30
+    per_row = hidden * (4 * element_size + 5 * 4) * 2
+    fit = max(ROW_BLOCK, (avail // 2 // per_row) // ROW_BLOCK * ROW_BLOCK)
+    return min(rows, fit)
+
+
+def ako_reference_cpu(rows: int, hidden: int, dtype: torch.dtype, warmup: int, repeats: int) -> dict:
+    """AKO's ``rmsnorm_residual_ref`` on CPU tensors of ``rows`` rows drawn
+    like the workload's (N(0, 1) rows, N(1, 0.1) weight, from the CPU
+    generator: the same distribution, not the GPU arm's bytes, which a
+    memory-bound op's time does not depend on), timed with AKO's
+    ``bench_op`` (wall clock on CPU, one call per timed batch, p50)."""
+    from ako_b200.reference import ako
+
+    ako()
+    from ako.benchmark.bench_op import bench_op
+    from ako.ops.rmsnorm_ref import rmsnorm_residual_ref
+
+    x, r = global_rows(0, rows, hidden, dtype, "cpu", 0)
+    w = weight(hidden, dtype, "cpu", 0)
+    res = bench_op(rmsnorm_residual_ref, (x, r, w), call_kwargs={"eps": 1e-5}, warmup=warmup, repeats=repeats,
+                   inner=1, kernel_name="rmsnorm_residual_ref")
+    b = x.element_size()
+    nbytes = 4 * rows * hidden * b + hidden * b
+    return {"value": round(nbytes / (res.latency_p50_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"{rows} x {hidden} {str(dtype).replace('torch.', '')} rows per call; AKO's "
+                      f"ako.ops.rmsnorm_ref.rmsnorm_residual_ref on CPU tensors, timed by ako.benchmark.bench_op "
+                      f"(warmup {warmup}, {repeats} timed calls, p50 {res.latency_p50_ms:.1f} ms)",
+            "ms_per_call": round(res.latency_p50_ms, 3), "bytes_per_call": nbytes, **cpu_description()}
+
+
+
+def c_port_cpu(rows: int, hidden: int, dtype: torch.dtype, seconds: float) -> dict:
+    """The C restatement of AKO's reference (``oracle/ako_oracle.c``, all host
+    threads) on ``rows`` rows drawn like the workload's."""
+    import numpy as np
+
+    from oracle import c_oracle as C
+
+    x, r = global_rows(0, rows, hidden, dtype, "cpu", 0)
+    w = weight(hidden, dtype, "cpu", 0)
+    host = lambda t: t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()  # noqa: E731
+    xn, rn, wn = host(x), host(r), host(w)
+    name = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.float32: "float32"}[dtype]
+    threads = C.default_threads()
+    C.rmsnorm_residual(xn, rn, wn, 1e-5, name, threads=threads)  # page in, start threads
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        C.rmsnorm_residual(xn, rn, wn, 1e-5, name, threads=threads)
+        calls += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    b = x.element_size()
+    return {"value": round((4 * rows * hidden + hidden) * b * calls / dt / 1e9, 3), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{rows} x {hidden} rows per call, {calls} calls in {dt:.1f} s "
+                      f"(C restatement of AKO's reference, oracle/ako_oracle.c, pthreads)"}
+
+
 # ---------------------------------------------------------------- extras
 def run_ops(device: torch.device, peak: float) -> dict:
     from ako_b200.benchmark.timing import Flusher, cold_us
@@ -227,29 +406,44 @@ def run_ops(device: torch.device, peak: float) -> dict:
     return out
 
 
-def cpu_baseline(wl: Workload, seconds: float, sample_rows: int | None = None) -> dict:
-    """C oracle (restated reference, all host threads) on a row sample of the workload."""
-    from oracle import c_oracle as C
+def run_decoder(reps: int) -> dict:
+    """Configuration 5 on this GPU: the B200 decoder and the same stack on the
+    reference math (``ako_b200.benchmark.decoder_bench``)."""
+    from ako_b200.benchmark import decoder_bench
 
-    m, h = wl.dims
-    b = wl.x.element_size()
-    rows = sample_rows or max(1, min(m, (256 << 20) // (4 * h * b)))
-    to_np = lambda t: t.cpu().view(torch.int16).numpy().view("uint16") if t.dtype == torch.bfloat16 else t.cpu().numpy()  # noqa: E731
-    x, r, w = to_np(wl.x[:rows]), to_np(wl.r[:rows]), to_np(wl.w)
-    dtype = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.float32: "float32"}[wl.dtype]
-    threads = C.default_threads()
-    C.rmsnorm_residual(x, r, w, 1e-5, dtype, threads=threads)  # warm (page in, thread start)
-    calls, t0 = 0, time.perf_counter()
-    while True:
-        C.rmsnorm_residual(x, r, w, 1e-5, dtype, threads=threads)
-        calls += 1
-        if time.perf_counter() - t0 >= seconds:
-            break
-    dt = time.perf_counter() - t0
-    bytes_ = (4 * rows * h + h) * b * calls
-    return {"value": round(bytes_ / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"rows 0..{rows - 1} of the {m}x{h} {dtype} workload, {calls} calls in {dt:.1f} s "
-                      f"(C oracle, pthreads)"}
+    args = argparse.Namespace(layers=4, prefill_batch=8, prefill_len=2048, decode_batch=32, decode_steps=128,
+                              context=2048, warmup=2, reps=reps)
+    res = decoder_bench.run(args)
+    out = {"prefill_tok_s": res["b200"]["prefill_tok_s"], "decode_tok_s": res["b200"]["decode_tok_s"],
+           "decode_graph_tok_s": res["b200"]["decode_graph_tok_s"], "b200": res["b200"],
+           "reference_math": res["torch"], "parity": res["parity"],
+           "speedup_vs_reference_math": res["speedup_vs_reference_math"],
+           "config": "4 layers, d 4096, 32/8 heads, FFN 11008, bf16, N(0, 0.02) weights; prefill 8 x 2048; "
+                     "decode 32 x 128 steps from a 2048-token cache; GEMMs and attention are torch's"}
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ako_decoder() -> dict:
+    """AKO's own decoder stack through AKO's selector, each mode in a fresh
+    process with an empty kernel cache (``ako_b200.benchmark.ako_decoder``)."""
+    import subprocess
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        out = Path(tmp) / "ako_decoder.json"
+        proc = subprocess.run([sys.executable, "-m", "ako_b200.benchmark.ako_decoder", "--reps", "3",
+                               "--out", str(out)], cwd=str(REPO), capture_output=True, text=True, check=False)
+        if proc.returncode != 0:
+            return {"error": f"status {proc.returncode}: {proc.stderr.strip().splitlines()[-1:]}"}
+        doc = json.loads(out.read_text())
+    summary = {}
+    for r in doc["results"]:
+        chosen = [s["kernel"] for s in r.get("selections", [])]
+        summary[r["mode"]] = {"prefill_tok_s": r["prefill_tok_s"], "decode_tok_s": r["decode_tok_s"],
+                              "prefill_ms": r["prefill_ms"], "decode_ms_per_step": r["decode_ms_per_step"],
+                              "selected": {k: chosen.count(k) for k in sorted(set(chosen))}}
+    return summary
 
 
 # ---------------------------------------------------------------- reference
@@ -257,44 +451,27 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU reference runs once, on rank 0
-    from oracle import c_oracle as C
-    import numpy as np
-
     op, (m, h), dt = WORKLOADS[args.workload]
     if op != "rmsnorm_residual":
         raise SystemExit("--impl reference supports the rmsnorm_residual workloads")
-    b = 2
-    # ~256 MB of traffic per step, the cpu_baseline leg's sample: smaller
-    # steps spend a larger share on starting the threads and touching fresh
-    # output pages, which would understate the CPU's throughput.
-    rows = max(1, min(m, (256 << 20) // (4 * h * b)))
-    from oracle.ako_oracle import encode
-
-    rng = np.random.default_rng(0)
-    x = encode(rng.standard_normal((rows, h), dtype=np.float32), "bfloat16")
-    r = encode(rng.standard_normal((rows, h), dtype=np.float32), "bfloat16")
-    w = encode(rng.standard_normal(h, dtype=np.float32) * np.float32(0.1) + np.float32(1.0), "bfloat16")
-    threads = C.default_threads()
-    step = lambda: C.rmsnorm_residual(x, r, w, 1e-5, "bfloat16", threads=threads)  # noqa: E731
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = time.perf_counter() - t0
-    step_bytes = (4 * rows * h + h) * b
-    value = step_bytes * args.steps / dt / 1e9
+    rows = host_rows_that_fit(m, h, torch.tensor([], dtype=dt).element_size())
+    if args.reference_rows:
+        rows = min(rows, args.reference_rows)
+    ref = ako_reference_cpu(rows, h, dt, args.warmup, args.steps)
+    port = c_port_cpu(rows, h, dt, min(10.0, args.cpu_seconds)) if not args.no_cpu else None
+    value = ref["value"]
     line = {
-        "impl": "reference", "metric": "achieved HBM GB/s", "value": round(value, 3), "unit": "GB/s",
+        "impl": "reference", "metric": "achieved HBM GB/s", "value": value, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1000 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "op": op, "rows_per_gpu": m, "hidden": h,
-                   "step": f"{rows}-row sample of the workload per step (bounded CPU work)"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} x {h} bf16 rows per step; C restatement of AKO's unfused "
-                                   f"reference (oracle/ako_oracle.c), pthreads"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "ms_per_step": ref["ms_per_call"], "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) rows, weight N(1,0.1))",
+        "config": {"workload": args.workload, "op": op, "rows": m, "hidden": h,
+                   "step": f"one call of AKO's rmsnorm_residual_ref on CPU tensors of {rows} x {h} rows "
+                           f"({'the whole batch' if rows == m else 'the rows host memory holds'}), drawn like the "
+                           f"GPU arm's (seeded N(0,1) rows, N(1,0.1) weight, CPU generator)"},
+        "cpu_baseline": {k: v for k, v in ref.items() if k not in ("ms_per_call", "bytes_per_call")},
+        "c_port": port,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -307,11 +484,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--scaling", choices=("strong", "weak"), default="strong",
+                    help="strong: one global batch split over the ranks; weak: a whole batch per rank")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer leg (default: --steps, max 20)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--reference-rows", type=int, default=None,
+                    help="cap on the rows AKO's CPU reference runs on (default: as many as host memory holds)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ops", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--no-ako-decoder", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -320,21 +503,39 @@ def main() -> None:
         run_reference(args)
         return
 
+    from ako_b200 import _native, sharding
+    from ako_b200.benchmark.clocks import start_sampler
+
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     peak, peak_src = hbm_peak()
+    op, dims, _ = WORKLOADS[args.workload]
+    row_op = op in ("rmsnorm", "rmsnorm_residual")
+    strong = args.scaling == "strong" and row_op
+    shard = sharding.shard_range(dims[0], world, rank) if strong else None
 
-    from ako_b200.benchmark.clocks import start_sampler
-
-    wl = Workload(args.workload, device, seed=rank)
+    wl = Workload(args.workload, device, seed=0, rows=shard)
     sampler = start_sampler(local)
-    ms = timed_region(wl.step, args.steps, args.warmup, world, marks=sampler)
+    ms = timed_region(wl.step, args.steps, args.warmup, marks=sampler)
     clocks = sampler.stop()
-    ms_max = max_over_ranks(ms, world, device)
+    ms_max = sharding.max_over_ranks(ms, device)
     per_step_ms = ms_max / args.steps
-    total_bytes = wl.bytes * world
-    value = total_bytes / (per_step_ms * 1e-3) / 1e9
+    step_bytes = sharding.sum_over_ranks(wl.bytes, device)  # the global batch (strong) or N batches (weak)
+    value = step_bytes / (per_step_ms * 1e-3) / 1e9
     achieved = wl.bytes / ((ms / args.steps) * 1e-3) / 1e9  # this rank's kernel
+    parity = shard_parity(wl) if row_op else None
+    parity_all = sharding.all_over_ranks(parity["ok"], device) if parity is not None else None
+
+    weak = None
+    if world > 1 and strong:
+        full = Workload(args.workload, device, seed=rank + 1)
+        wms = timed_region(full.step, args.steps, args.warmup)
+        wmax = sharding.max_over_ranks(wms, device)
+        weak = {"value": round(full.bytes * world / (wmax / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(wmax / args.steps, 4),
+                "config": f"a whole {dims[0]}-row batch on every rank ({world} batches per step)"}
+        del full
+        torch.cuda.empty_cache()
 
     e2e = None
     if not args.no_e2e and wl.op == "rmsnorm_residual":
@@ -348,31 +549,41 @@ def main() -> None:
         xh.copy_(wl.x)
         rh.copy_(wl.r)
         e2e_step = lambda: host.rmsnorm_residual_host(xh, rh, wl.w, 1e-5, y_out=yh, residual_out=roh)  # noqa: E731
-        ems = timed_region(e2e_step, k, 3, world)
-        ems_max = max_over_ranks(ems, world, device)
-        m, h = wl.dims
-        io = 2 * m * h * wl.x.element_size()
-        e2e = {"value": round(total_bytes / (ems_max / k * 1e-3) / 1e9, 2), "unit": "GB/s",
-               "h2d_bytes_per_step": io, "d2h_bytes_per_step": io, "steps": k,
+        ems = timed_region(e2e_step, k, 3)
+        ems_max = sharding.max_over_ranks(ems, device)
+        n, h = wl.x.shape
+        io = 2 * n * h * wl.element_size
+        e2e = {"value": round(step_bytes / (ems_max / k * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": io * world, "d2h_bytes_per_step": io * world, "steps": k,
                "ms_per_step": round(ems_max / k, 3),
                "api": "ako_b200.host.rmsnorm_residual_host (pinned host buffers, chunked H2D/kernel/D2H "
                       "on three streams, C-ABI ako_b200_rmsnorm_residual per chunk)",
-               "gpu_launches": k * host.launches_per_call(m, h, wl.x.element_size())}
+               "gpu_launches": k * world * host.launches_per_call(n, h, wl.element_size)}
         del xh, rh, yh, roh
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu and wl.op == "rmsnorm_residual":
-        cpu = cpu_baseline(wl, args.cpu_seconds)
-
-    ops = None
-    if world == 1 and not args.no_ops:
-        ops = run_ops(device, peak)
-
-    from ako_b200 import sharding
-
+    # Every rank has finished its GPU work with the same collective steps; the
+    # legs below run on rank 0 alone at N = 1.
+    device_status = _native.take_device_status()
     sharding.finish()
     if rank != 0:
         return
+
+    # GPU legs first: the CPU legs leave torch's intra-op threads spinning,
+    # which slows the host's launches of short kernels that follow.
+    ops = run_ops(device, peak) if world == 1 and not args.no_ops else None
+    decoder = None
+    if world == 1 and not args.no_decoder:
+        decoder = run_decoder(reps=5)
+        if not args.no_ako_decoder:
+            decoder["ako_stack_through_akos_selector"] = run_ako_decoder()
+
+    cpu = None
+    if world == 1 and not args.no_cpu and wl.op == "rmsnorm_residual":
+        m, h = dims
+        rows = min(host_rows_that_fit(m, h, wl.element_size), 8192)
+        cpu = ako_reference_cpu(rows, h, wl.dtype, warmup=1, repeats=3)
+        cpu.pop("bytes_per_call", None)
+        cpu["port"] = c_port_cpu(min(rows, 2048), h, wl.dtype, args.cpu_seconds)
 
     traffic = ncu_traffic(args.workload)
     line = {
@@ -384,17 +595,19 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": round(per_step_ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if wl.dtype == torch.bfloat16 else str(wl.dtype).replace("torch.", ""),
-        "data": "synthetic (seeded N(0,1) inputs, weight N(1,0.1), generated on device)",
+        "data": "synthetic (seeded N(0,1) rows, weight N(1,0.1), generated on device by global row index)",
         "config": {
             "workload": args.workload,
             "op": wl.op,
-            **{f"{k}_per_gpu" if k == "rows" else k: v for k, v in wl.desc.items()},
-            "bytes_per_step_per_gpu": wl.bytes,
-            "l2": "inputs larger than L2 (step moves far more than the 126 MB L2); no flush",
-            "parallelism": f"row-sharded x{world}, no collective (weak scaling)",
+            **({"global_rows": dims[0], "rows_per_gpu": wl.hi - wl.lo, "hidden": dims[1]} if row_op else wl.desc),
+            "bytes_per_step": step_bytes,
+            "l2": "inputs larger than L2 (the step moves far more than the 126 MB L2); no flush",
+            "parallelism": (f"one {dims[0]}-row batch split into {world} contiguous row blocks "
+                            f"(ako_b200.sharding.shard_range), no collective on the data path" if strong else
+                            f"a whole batch per rank x{world}, no collective on the data path"),
         },
         "roofline": {
             "bound": "hbm",
@@ -402,19 +615,25 @@ def main() -> None:
             "peak": peak,
             "unit": "GB/s",
             "frac": round(achieved / peak, 4),
-            "traffic": traffic,
+            "traffic": traffic if world == 1 or not strong else None,
             "peak_source": peak_src,
             "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-            "kernel": "ako_b200::rms_rows_kernel (CUDA events over the timed steps, launching stream)",
+            "kernel": f"{wl.kernel} (CUDA events over the timed steps, launching stream, rank 0)",
         },
+        "parity": ({**parity, "ok_all_ranks": parity_all} if parity is not None else None),
+        "device_status": device_status,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clocks,
-        "gpu_launches": args.steps * wl.launches_per_step,
+        "gpu_launches": args.steps * world,
         "gpu_name": torch.cuda.get_device_name(device),
     }
+    if weak is not None:
+        line["weak"] = weak
     if ops is not None:
         line["ops"] = ops
+    if decoder is not None:
+        line["decoder"] = decoder
     print(json.dumps(line), flush=True)
 
 

@@ -1,6 +1,7 @@
-"""CPU tests of the measurement tools: the reference arm of ``bench.py`` (the
-C oracle on the host cores) keeps the JSON line contract, ``bench.py``
-refuses fewer than 3 warm-up steps, and the sweep report renders its tables
+"""CPU tests of the measurement tools: the reference arm of ``bench.py`` (AKO's
+own reference on the host cores, with the C restatement beside it) keeps the
+JSON line contract, ``bench.py`` refuses fewer than 3 warm-up steps, the
+global batch's shards are its rows, and the sweep report renders its tables
 and counts from a sweep JSON."""
 
 from __future__ import annotations
@@ -9,6 +10,8 @@ import json
 import subprocess
 import sys
 from pathlib import Path
+
+import torch
 
 from ako_b200.benchmark.sweep import cell_label, report
 
@@ -21,7 +24,8 @@ def _bench(*args: str, timeout: int = 240) -> subprocess.CompletedProcess:
 
 
 def test_reference_arm_json_line() -> None:
-    proc = _bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+    proc = _bench("--impl", "reference", "--steps", "1", "--warmup", "3", "--reference-rows", "1024",
+                  "--cpu-seconds", "1")
     assert proc.returncode == 0, proc.stderr[-2000:]
     lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1, proc.stdout
@@ -31,7 +35,9 @@ def test_reference_arm_json_line() -> None:
     assert rec["value"] > 0 and rec["steps"] == 1 and rec["warmup"] == 3 and rec["n_gpus"] == 1
     assert rec["config"]["workload"] == "rmsnorm_residual_bf16_32768x16384"
     cb = rec["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == rec["value"] and cb["sample"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["value"] == rec["value"] and cb["sample"]
+    assert "rmsnorm_residual_ref" in cb["sample"] and cb["cpu_model"] is not None and cb["torch_threads"] >= 1
+    assert rec["c_port"]["kind"] == "port" and rec["c_port"]["value"] > 0
     assert rec["e2e"] == {"value": rec["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
@@ -69,7 +75,11 @@ def test_sweep_report_tables_and_counts() -> None:
     assert "| rmsnorm_residual | 1 | 1/1, x1.20 | 1/1, x2.00 | 1/1, x4.00 |" in md
     for cfg in ("## Config 1", "## Config 2", "## Config 3", "## Config 4", "## Decode cells"):
         assert cfg in md
-    assert "| fp32 | M2048 H4096 | 10 | 100 | 0.500 | 0.90 | 2.00 | 4.00 | 2 |" in md
+    assert "| fp32 | M2048 H4096 | 10 | - | 100 | 0.500 | 0.90 | 2.00 | 4.00 | 2 |" in md
+    # with a time launched like the competitors (no programmatic launch), ratios use it
+    md2 = report({"peak_gbs": 6542.7, "reference_package": True, "launches": 20, "blocks": 7,
+                  "cells": [_cell("rmsnorm", dtype="fp32", rows=2048, hidden=4096, triton_us=9.0, ours_nopdl_us=12.0)]})
+    assert "| fp32 | M2048 H4096 | 10 | 12 | 100 | 0.500 | 0.75 | 1.67 | 3.33 |" in md2
     assert "- vs triton: wall clock, ours faster on 1 of 1 cells (x2.00); in a graph, ours at or below on 0 of 1" in md
 
 
@@ -114,3 +124,29 @@ def test_sweep_cells_cover_the_benchmark_grid() -> None:
     assert {(c["rows"], c["hidden"], c["packed"]) for c in by[4]} == {
         (m, f, p) for m in (1, 64, 2048, 16384) for f in (5632, 11008, 14336) for p in (False, True)}
     assert all(c["decode"] == (c["rows"] <= 64) for c in by[4])
+
+
+def test_shards_of_the_global_batch_are_its_rows() -> None:
+    """Each rank generates only its rows, from seeds indexed by global row
+    block, so the shards of any GPU count concatenate to the one-GPU batch."""
+    import bench
+    from ako_b200.sharding import shard_range
+
+    m, h = 5000, 16
+    whole_x, whole_r = bench.global_rows(0, m, h, torch.bfloat16, "cpu", 0)
+    for world in (2, 3, 8):
+        parts = [bench.global_rows(*shard_range(m, world, r), h, torch.bfloat16, "cpu", 0) for r in range(world)]
+        assert torch.equal(torch.cat([p[0] for p in parts]), whole_x)
+        assert torch.equal(torch.cat([p[1] for p in parts]), whole_r)
+    assert not torch.equal(whole_x[:1024], whole_r[:1024])
+    w = bench.weight(h, torch.float32, "cpu", 0)
+    assert abs(w.mean().item() - 1.0) < 0.1
+
+
+def test_host_rows_that_fit_is_bounded() -> None:
+    import bench
+
+    rows = bench.host_rows_that_fit(32768, 16384, 2)
+    assert bench.ROW_BLOCK <= rows <= 32768 and rows % bench.ROW_BLOCK == 0
+    desc = bench.cpu_description()
+    assert desc["os_cpu_count"] >= 1 and desc["torch_threads"] >= 1
