@@ -61,7 +61,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                     ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
                                     ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "ako_b200_swiglu_plan": (_c_int, [ctypes.c_int64, ctypes.c_int64, _c_int, _c_int, _c_int,
-                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
+                                      ctypes.POINTER(_c_int)]),
     "ako_b200_rmsnorm_plan": (_c_int, [ctypes.c_int64, ctypes.c_int64, _c_int, _c_int, _c_int,
                                        ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
                                        ctypes.POINTER(_c_int)]),
@@ -75,10 +76,11 @@ MEASURE_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ako_b200_measure_set_wait_polls": (ctypes.c_uint, [ctypes.c_uint]),
     "ako_b200_rope_set_launch": (_c_int, [_c_int]),
     "ako_b200_swiglu_set_launch": (_c_int, [_c_int, _c_int]),
+    "ako_b200_swiglu_set_grid": (_c_int, [_c_int]),
     "ako_b200_set_pdl": (_c_int, [_c_int]),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Status codes (ako_b200_status).
 OK = 0

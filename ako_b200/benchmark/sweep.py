@@ -14,7 +14,10 @@ competitors; the kernel-to-kernel comparison uses the second. Decode cells
 (one token per sequence) add the wall-clock latency per call of back-to-back
 calls, which is what a decode loop pays, and the device time per call of 20
 calls captured in one CUDA graph. Each cell is also checked against AKO's
-eager reference with AKO's error budget.
+eager reference with AKO's error budget, and timed against a plain
+device-to-device copy of its algorithmic bytes (half read, half written),
+timed the same way: the practical roofline at that size, since ramp-up, the
+last wave and the final write-back cost a fixed few microseconds.
 
     python -m ako_b200.benchmark.sweep --out sweep.json [--configs 1,2,3,4]
     python -m ako_b200.benchmark.sweep --report sweep.json > sweep.md
@@ -226,7 +229,9 @@ def report(summary: dict[str, Any]) -> str:
            "- `us nopdl`: ours through the measurement build with programmatic dependent launch off, launched",
            "  like the competitors. `x` columns and the summary compare each competitor with it (above 1: ours",
            "  is faster); `us` is ours as shipped (programmatic launch on).",
-           "- `ulps`: AKO's `error_in_ulps` of our output against its eager reference.", ""]
+           "- `ulps`: AKO's `error_in_ulps` of our output against its eager reference.",
+           "- `copy`: a plain device-to-device copy of the cell's algorithmic bytes, timed the same way; `us/copy` is",
+           "  ours (as shipped) over it: the practical roofline at that size.", ""]
     fails = [c for c in cells if not c["parity"]]
     out.append(f"All {len(cells)} cells pass AKO's error budget." if not fails else
                f"{len(fails)} of {len(cells)} cells fail AKO's error budget: " +
@@ -236,6 +241,10 @@ def report(summary: dict[str, Any]) -> str:
         maxu[c["op"]] = max(maxu.get(c["op"], 0.0), c["ulps"])
     out.append("Max reported ulps: " + ", ".join(f"{op} {u:g}" + (" (bit-exact)" if u == 0 else "")
                                                  for op, u in maxu.items()) + ".")
+    vs_copy = [c["ours_us"] / c["copy_us"] for c in cells if c.get("copy_us") and not c.get("decode")]
+    if vs_copy:
+        out.append(f"Throughput cells against a copy of the same bytes: at most {max(vs_copy):.2f}x its time, "
+                   f"geometric mean {_geomean(vs_copy):.2f}x.")
     out.append("")
     out.append("Throughput cells (not decode), ours against each competitor: cells where ours is at or below "
                "its time, and the geometric mean of its time over ours.")
@@ -254,15 +263,16 @@ def report(summary: dict[str, Any]) -> str:
     out.append("")
     for cfg in sorted({c["config"] for c in cells}):
         out += [f"## {TITLES[cfg]}", "",
-                "| dtype | cell | us | us nopdl | GB/s | frac | " + " | ".join(f"x {n}" for n in COMPETITORS)
+                "| dtype | cell | us | us nopdl | GB/s | frac | us/copy | " + " | ".join(f"x {n}" for n in COMPETITORS)
                 + " | ulps |",
-                "|---|---|---:|---:|---:|---:|" + "---:|" * len(COMPETITORS) + "---:|"]
+                "|---|---|---:|---:|---:|---:|---:|" + "---:|" * len(COMPETITORS) + "---:|"]
         for c in cells:
             if c["config"] != cfg:
                 continue
             xs = " | ".join(f"{r:.2f}" if (r := _ratio(c, n)) else "-" for n in COMPETITORS)
+            vc = f"{c['ours_us'] / c['copy_us']:.2f}" if c.get("copy_us") else "-"
             out.append(f"| {c['dtype']} | {cell_label(c)} | {_fmt(c['ours_us'])} | {_fmt(c.get('ours_nopdl_us'))} | "
-                       f"{c['ours_gbs']:.0f} | {c['frac']:.3f} | {xs} | {c['ulps']:g} |")
+                       f"{c['ours_gbs']:.0f} | {c['frac']:.3f} | {vc} | {xs} | {c['ulps']:g} |")
         out.append("")
     dec = [c for c in cells if c.get("decode")]
     if dec:
@@ -336,6 +346,11 @@ def main() -> None:
         row["ours_us"] = round(us, 3)
         row["ours_gbs"] = round(nbytes / us / 1e3, 1)
         row["frac"] = round(nbytes / us / 1e3 / peak, 4)
+        half = max(16, nbytes // 2)
+        src = torch.empty(half, dtype=torch.uint8, device=dev)
+        dst = torch.empty_like(src)
+        row["copy_us"] = round(device_us(dst.copy_, (src,), args.launches, flush, args.blocks), 3)
+        del src, dst
         with _native.measurement() as mlib:
             mlib.ako_b200_set_pdl(0)
             try:

@@ -42,10 +42,12 @@ struct SwigluArgs {
 constexpr int kThreads = 256;  // default CTA size
 constexpr int64_t kTinyElements = int64_t{1} << 15;  // up to this many: 4-byte accesses
 
-// Tuning overrides of the CTA size and of the vectors in flight per thread
-// (0: built-in choice). Measurement builds only.
+// Tuning overrides of the CTA size, of the vectors in flight per thread and
+// of the grid's thread budget per SM (0: built-in choice). Measurement builds
+// only.
 AKO_B200_OVERRIDE int g_threads = 0;
 AKO_B200_OVERRIDE int g_unroll = 0;
+AKO_B200_OVERRIDE int g_threads_per_sm = 0;
 
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
@@ -143,11 +145,14 @@ __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
     }
 }
 
+// The grid strides over the vectors with at most `threads_per_sm` threads
+// per SM (CTAs of THREADS threads).
 template <typename T, int VEC, int UNROLL, int THREADS>
-int launch(SwigluArgs a, bool flat, cudaStream_t st) {
+int launch(SwigluArgs a, bool flat, int threads_per_sm, cudaStream_t st) {
     const int64_t per_cta = static_cast<int64_t>(THREADS) * UNROLL;
     int64_t grid = (a.total + per_cta - 1) / per_cta;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / THREADS);  // a full SM's worth of threads each
+    const int ctas_per_sm = threads_per_sm >= THREADS ? threads_per_sm / THREADS : 1;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * ctas_per_sm;
     if (grid > cap) grid = cap;
     const dim3 g(static_cast<unsigned>(grid));
     if (flat) return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
@@ -162,8 +167,12 @@ int launch(SwigluArgs a, bool flat, cudaStream_t st) {
 // problems, or the element size when the operands are not 16-byte aligned),
 // CTA size and vectors per thread.
 struct SwigluPlan {
-    int access_bytes, threads, unroll;
+    int access_bytes, threads, unroll, threads_per_sm;
 };
+
+// Thread budget per SM of the grid-stride grid, built-in: a full SM of
+// threads.
+constexpr int kThreadsPerSm = 2048;
 
 SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat) {
     if (vector_ok && g_threads == 0 && rows * h <= kTinyElements) {
@@ -173,7 +182,7 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // reciprocals. In CUDA graphs on B200 this is 0.1 us faster per call
         // for fp16 and fp32 rows of 5632-14336 at 1-2 rows and the same for
         // bf16; above 2^15 elements 16-byte accesses are as fast or faster.
-        return SwigluPlan{4, 128, 1};
+        return SwigluPlan{4, 128, 1, kThreadsPerSm};
     }
     if (vector_ok) {
         // 256-thread CTAs with one vector of each input per thread (32
@@ -184,25 +193,38 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // with two. Small problems (decode rows) use 128-thread CTAs, so the
         // few vectors spread over many SMs (measured fastest up to ~64 rows of
         // 5632..14336).
+        //
+        // Strided operands (the packed [M, 2F] halves) of 2^24 vectors and more
+        // stream fastest with two vectors per thread and at most 1024 threads
+        // per SM: 2-3% faster than one vector and a full SM of threads on
+        // every such cell measured on B200 (F 11008 and 14336, 16384 rows,
+        // bf16 and fp16; e.g. bf16 16384 x 14336 packed 224.9 -> 218.5 us).
+        // The strided kernel with two vectors takes 48 registers, so a full
+        // SM's budget of 256-thread CTAs leaves 5 resident and the rest to a
+        // second, uneven pass; with 1024 threads all are resident. Dense
+        // operands keep two vectors and the full budget (59 registers: 4
+        // resident CTAs, two even passes), measured equal or faster.
         const int64_t total = rows * (h * es / 16);
         const bool small = total < static_cast<int64_t>(sm_count()) * kThreads * 4;
-        const bool huge_dense = flat && total >= (int64_t{1} << 24);
+        const bool huge = total >= (int64_t{1} << 24);
         return SwigluPlan{16, g_threads > 0 ? g_threads : (small ? 128 : kThreads),
-                          g_unroll > 0 ? g_unroll : (huge_dense ? 2 : 1)};
+                          g_unroll > 0 ? g_unroll : (huge ? 2 : 1),
+                          g_threads_per_sm > 0 ? g_threads_per_sm : (huge && !flat ? 1024 : kThreadsPerSm)};
     }
-    return SwigluPlan{es, 256, 4};
+    return SwigluPlan{es, 256, 4, kThreadsPerSm};
 }
 
 template <typename T, int VEC>
-int launch_vec(const SwigluArgs& a, bool flat, int threads, int unroll, cudaStream_t st) {
-    switch (threads * 16 + unroll) {
-        case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, st);
-        case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, st);
-        case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, st);
-        case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, st);
-        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, st);
-        case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, st);
-        default: return launch<T, VEC, 2, 256>(a, flat, st);
+int launch_vec(const SwigluArgs& a, bool flat, const SwigluPlan& p, cudaStream_t st) {
+    const int tps = p.threads_per_sm;
+    switch (p.threads * 16 + p.unroll) {
+        case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, tps, st);
+        case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, tps, st);
+        case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, tps, st);
+        case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, tps, st);
+        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, tps, st);
+        case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, tps, st);
+        default: return launch<T, VEC, 2, 256>(a, flat, tps, st);
     }
 }
 
@@ -213,9 +235,9 @@ int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaSt
     const int per_access = p.access_bytes / static_cast<int>(sizeof(T));
     a.per_row = h / per_access;
     a.total = rows * a.per_row;
-    if (!vector_ok) return launch<T, 1, 4, 256>(a, flat, st);
-    if (p.access_bytes == 4) return launch<T, 4 / sizeof(T), 1, 128>(a, flat, st);
-    return launch_vec<T, VEC>(a, flat, p.threads, p.unroll, st);
+    if (!vector_ok) return launch<T, 1, 4, 256>(a, flat, p.threads_per_sm, st);
+    if (p.access_bytes == 4) return launch<T, 4 / sizeof(T), 1, 128>(a, flat, p.threads_per_sm, st);
+    return launch_vec<T, VEC>(a, flat, p, st);
 }
 
 }  // namespace
@@ -255,9 +277,9 @@ extern "C" int ako_b200_swiglu(const void* gate, int64_t gate_row_stride, const 
 }
 
 extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int aligned, int dense,
-                                    int* access_bytes, int* threads, int* vectors_per_thread) {
+                                    int* access_bytes, int* threads, int* vectors_per_thread, int* threads_per_sm) {
     clear_error();
-    if (access_bytes == nullptr || threads == nullptr || vectors_per_thread == nullptr)
+    if (access_bytes == nullptr || threads == nullptr || vectors_per_thread == nullptr || threads_per_sm == nullptr)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_swiglu_plan: null output pointer");
     const int es = dtype_size(dtype);
     if (es == 0) return set_error(AKO_B200_ERR_UNSUPPORTED_DTYPE, "ako_b200_swiglu_plan: unsupported dtype code %d", dtype);
@@ -268,6 +290,7 @@ extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtyp
     *access_bytes = p.access_bytes;
     *threads = p.threads;
     *vectors_per_thread = p.unroll;
+    *threads_per_sm = p.threads_per_sm;
     return AKO_B200_OK;
 }
 
@@ -282,6 +305,15 @@ extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {
                          threads, vectors_per_thread);
     g_threads = threads;
     g_unroll = vectors_per_thread;
+    return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_swiglu_set_grid(int threads_per_sm) {
+    clear_error();
+    if (threads_per_sm != 0 && (threads_per_sm < 64 || threads_per_sm > 2048 || threads_per_sm % 64 != 0))
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT,
+                         "swiglu grid budget must be 0 or a multiple of 64 in [64, 2048], got %d", threads_per_sm);
+    g_threads_per_sm = threads_per_sm;
     return AKO_B200_OK;
 }
 #endif  // AKO_B200_MEASUREMENT

@@ -58,7 +58,7 @@ typedef enum {
 } ako_b200_rope_style;
 
 /* ABI version of this header; bumped on any signature change. */
-#define AKO_B200_ABI_VERSION 3
+#define AKO_B200_ABI_VERSION 4
 
 int ako_b200_abi_version(void);
 
@@ -231,14 +231,16 @@ int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_heads, int64_t 
  * The launch a SwiGLU call of `n_rows` x `hidden_dim` in `dtype` would get,
  * without launching anything (host only; no GPU needed): bytes per access
  * (16; 4 for decode-sized problems; the element size when the operands are
- * not 16-byte aligned), threads per CTA and vectors per thread. `aligned`
+ * not 16-byte aligned), threads per CTA, vectors per thread, and the grid's
+ * budget of threads per SM (the grid strides over the problem with at most
+ * that many threads on each SM). `aligned`
  * says whether the call's pointers and row strides are 16-byte aligned,
  * `dense` whether all three operands are contiguous. Follows the library's
  * built-in choice (in the measurement build, any override in force). Not
  * part of the reference's interface; it has no counterpart there.
  */
 int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtype, int aligned, int dense,
-                         int* access_bytes, int* threads, int* vectors_per_thread);
+                         int* access_bytes, int* threads, int* vectors_per_thread, int* threads_per_sm);
 
 #ifdef __cplusplus
 }

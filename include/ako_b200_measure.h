@@ -65,6 +65,13 @@ int ako_b200_rope_set_launch(int heads_per_thread);
 int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
 
 /*
+ * SwiGLU grid budget: the grid-stride grid keeps at most `threads_per_sm`
+ * threads on each SM (a multiple of 64 in [64, 2048]); 0 restores the
+ * built-in choice.
+ */
+int ako_b200_swiglu_set_grid(int threads_per_sm);
+
+/*
  * Programmatic dependent launch: with `enable` = 1 (the built-in setting)
  * every kernel is launched with programmatic stream serialization, so it may
  * start while the previous kernel in the stream drains; it waits for that

@@ -71,7 +71,7 @@ def test_measurement_library_exports_both_headers(mlib) -> None:
 
 
 def test_abi_version(lib, mlib) -> None:
-    assert lib.ako_b200_abi_version() == mlib.ako_b200_abi_version() == _native.ABI_VERSION == 3
+    assert lib.ako_b200_abi_version() == mlib.ako_b200_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_status_strings(lib) -> None:

@@ -75,11 +75,13 @@ def test_sweep_report_tables_and_counts() -> None:
     assert "| rmsnorm_residual | 1 | 1/1, x1.20 | 1/1, x2.00 | 1/1, x4.00 |" in md
     for cfg in ("## Config 1", "## Config 2", "## Config 3", "## Config 4", "## Decode cells"):
         assert cfg in md
-    assert "| fp32 | M2048 H4096 | 10 | - | 100 | 0.500 | 0.90 | 2.00 | 4.00 | 2 |" in md
+    assert "| fp32 | M2048 H4096 | 10 | - | 100 | 0.500 | - | 0.90 | 2.00 | 4.00 | 2 |" in md
     # with a time launched like the competitors (no programmatic launch), ratios use it
     md2 = report({"peak_gbs": 6542.7, "reference_package": True, "launches": 20, "blocks": 7,
-                  "cells": [_cell("rmsnorm", dtype="fp32", rows=2048, hidden=4096, triton_us=9.0, ours_nopdl_us=12.0)]})
-    assert "| fp32 | M2048 H4096 | 10 | 12 | 100 | 0.500 | 0.75 | 1.67 | 3.33 |" in md2
+                  "cells": [_cell("rmsnorm", dtype="fp32", rows=2048, hidden=4096, triton_us=9.0, ours_nopdl_us=12.0,
+                                  copy_us=8.0)]})
+    assert "| fp32 | M2048 H4096 | 10 | 12 | 100 | 0.500 | 1.25 | 0.75 | 1.67 | 3.33 |" in md2
+    assert "at most 1.25x its time" in md2
     assert "- vs triton: wall clock, ours faster on 1 of 1 cells (x2.00); in a graph, ours at or below on 0 of 1" in md
 
 

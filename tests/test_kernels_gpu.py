@@ -392,9 +392,9 @@ def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
     for rows, f, dt, packed in ((16384, 14336, torch.bfloat16, False), (16384, 14336, torch.bfloat16, True),
                                 (64, 14336, torch.float16, False), (1, 14336, torch.float16, False),
                                 (7, 100, torch.bfloat16, False)):
-        out = [ctypes.c_int() for _ in range(3)]
+        out = [ctypes.c_int() for _ in range(4)]
         assert lib.ako_b200_swiglu_plan(rows, f, codes[dt], 1, int(not packed), *(ctypes.byref(o) for o in out)) == 0
-        access, threads, unroll = (o.value for o in out)
+        access, threads, unroll, _ = (o.value for o in out)
         both = torch.randn(rows, 2 * f, device=cuda_device).to(dt)
         g, u = (both[:, :f], both[:, f:]) if packed else (both[:, :f].contiguous(), both[:, f:].contiguous())
         got = _kernel_names(lambda: kernels.swiglu_cuda_sm100(g, u))

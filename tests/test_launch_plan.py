@@ -38,12 +38,14 @@ def _built_in_choice():
     """Overrides live in the measurement build only; reset them around each test."""
     m = _native.measure_lib()
     for f in (lambda: m.ako_b200_rmsnorm_set_launch(0, 0, 0), lambda: m.ako_b200_rmsnorm_set_staging(0, 0, 0),
-              lambda: m.ako_b200_swiglu_set_launch(0, 0), lambda: m.ako_b200_rope_set_launch(0)):
+              lambda: m.ako_b200_swiglu_set_launch(0, 0), lambda: m.ako_b200_rope_set_launch(0),
+              lambda: m.ako_b200_swiglu_set_grid(0)):
         f()
     yield
     m.ako_b200_rmsnorm_set_launch(0, 0, 0)
     m.ako_b200_rmsnorm_set_staging(0, 0, 0)
     m.ako_b200_swiglu_set_launch(0, 0)
+    m.ako_b200_swiglu_set_grid(0)
     m.ako_b200_rope_set_launch(0)
 
 
@@ -124,9 +126,9 @@ def test_invalid_arguments_are_rejected() -> None:
 
 
 def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool = True, lib=None
-                ) -> tuple[int, int, int]:
+                ) -> tuple[int, int, int, int]:
     lib = lib or _native.lib()
-    out = [ctypes.c_int() for _ in range(3)]
+    out = [ctypes.c_int() for _ in range(4)]
     rc = lib.ako_b200_swiglu_plan(rows, f, dtype, int(aligned), int(dense), *(ctypes.byref(o) for o in out))
     assert rc == 0, lib.ako_b200_last_error()
     return tuple(o.value for o in out)
@@ -135,15 +137,17 @@ def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool
 @pytest.mark.parametrize(
     "rows, f, dtype, aligned, dense, expected",
     [
-        (16384, 14336, BF16, True, True, (16, 256, 2)),   # 2^24.8 dense vectors: two per thread
-        (16384, 14336, BF16, True, False, (16, 256, 1)),  # packed halves (strided)
-        (2048, 11008, F16, True, True, (16, 256, 1)),
-        (64, 14336, BF16, True, True, (16, 128, 1)),      # decode rows: 128-thread CTAs
-        (1, 14336, F16, True, True, (4, 128, 1)),         # decode-sized: two elements per thread
-        (2, 16384, F32, True, True, (4, 128, 1)),         # 2^15 elements, the limit
-        (1, 32776, BF16, True, True, (16, 128, 1)),       # just above it
-        (7, 100, BF16, True, True, (2, 256, 4)),          # 200-byte rows: element accesses
-        (8, 4096, BF16, False, True, (2, 256, 4)),        # unaligned operands
+        (16384, 14336, BF16, True, True, (16, 256, 2, 2048)),   # 2^24.8 dense vectors: two per thread
+        (16384, 14336, BF16, True, False, (16, 256, 2, 1024)),  # packed halves (strided): two, 1024 threads/SM
+        (16384, 11008, F16, True, False, (16, 256, 2, 1024)),
+        (16384, 5632, BF16, True, False, (16, 256, 1, 2048)),   # below 2^24 vectors
+        (2048, 11008, F16, True, True, (16, 256, 1, 2048)),
+        (64, 14336, BF16, True, True, (16, 128, 1, 2048)),      # decode rows: 128-thread CTAs
+        (1, 14336, F16, True, True, (4, 128, 1, 2048)),         # decode-sized: two elements per thread
+        (2, 16384, F32, True, True, (4, 128, 1, 2048)),         # 2^15 elements, the limit
+        (1, 32776, BF16, True, True, (16, 128, 1, 2048)),       # just above it
+        (7, 100, BF16, True, True, (2, 256, 4, 2048)),          # 200-byte rows: element accesses
+        (8, 4096, BF16, False, True, (2, 256, 4, 2048)),        # unaligned operands
     ],
 )
 def test_swiglu_built_in_choice(rows, f, dtype, aligned, dense, expected) -> None:
@@ -153,9 +157,12 @@ def test_swiglu_built_in_choice(rows, f, dtype, aligned, dense, expected) -> Non
 def test_swiglu_override_is_followed() -> None:
     m = _native.measure_lib()
     assert m.ako_b200_swiglu_set_launch(64, 2) == 0
-    assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2)
-    assert swiglu_plan(1, 5632, BF16, lib=m) == (16, 64, 2)  # an override also skips the decode-sized path
-    assert swiglu_plan(2048, 11008, BF16) == (16, 256, 1)
+    assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2, 2048)
+    assert swiglu_plan(1, 5632, BF16, lib=m) == (16, 64, 2, 2048)  # an override also skips the decode-sized path
+    assert m.ako_b200_swiglu_set_grid(1536) == 0
+    assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2, 1536)
+    assert m.ako_b200_swiglu_set_grid(100) == 1 and m.ako_b200_swiglu_set_grid(0) == 0
+    assert swiglu_plan(2048, 11008, BF16) == (16, 256, 1, 2048)
 
 
 def rope_plan(b: int, s: int, h: int, d: int, style: int, dtype: int, lib=None) -> tuple[int, int, int, int, int]:
