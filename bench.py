@@ -88,7 +88,11 @@ WORKLOADS = {
     # small cases of the same kernels (a few hundred MB, above L2) for ncu captures
     "rmsnorm_residual_bf16_2048x16384": ("rmsnorm_residual", (2048, 16384), torch.bfloat16),
     "rmsnorm_residual_bf16_4096x4096": ("rmsnorm_residual", (4096, 4096), torch.bfloat16),
-    "rmsnorm_bf16_1024x65536": ("rmsnorm", (1024, 65536), torch.bfloat16),
+    "rmsnorm_bf16_1024x65536": ("rmsnorm", (1024, 65536), torch.bfloat16),   # chunked persistent kernel
+    "rmsnorm_bf16_1024x32768": ("rmsnorm", (1024, 32768), torch.bfloat16),   # staged persistent kernel
+    "rmsnorm_bf16_16384x4100": ("rmsnorm", (16384, 4100), torch.bfloat16),   # any-width kernel (8200-byte rows)
+    "rope_q_bf16_16x512x32x100": ("rope", (16, 512, 32, 100), torch.bfloat16),  # 4-byte accesses
+    "rope_q_bf16_16x512x32x98": ("rope", (16, 512, 32, 98), torch.bfloat16),    # one pair per thread
     "rope_q_bf16_16x512x32x128": ("rope", (16, 512, 32, 128), torch.bfloat16),
     "rope_qk_bf16_8x512x32+8x128": ("rope_qk", (8, 512, 32, 128), torch.bfloat16),
 }
@@ -291,17 +295,21 @@ def shard_parity(wl: Workload) -> dict:
     dt = {torch.bfloat16: O.BF16, torch.float16: O.F16, torch.float32: O.F32}[wl.dtype]
     xs, w = host(wl.x[sel]), host(wl.w)
     ok, worst = True, 0
+    # rows of whole 16-byte vectors run on the vector kernels, held to the fixed-order model
+    vectors = (xs.shape[-1] * xs.dtype.itemsize) % 16 == 0
     if wl.op == "rmsnorm_residual":
         rs = host(wl.r[sel])
         y, ro = (host(t[sel]) for t in wl.fn())
-        ym, rom = C.rmsnorm_fixed_order(xs, rs, w, 1e-5, dt)
         yo, roo = C.rmsnorm_residual(xs, rs, w, 1e-5, dt)
-        ok = bool(np.array_equal(y, ym) and np.array_equal(ro, rom) and np.array_equal(ro, roo))
+        ok = bool(np.array_equal(ro, roo))
+        if vectors:
+            ym, rom = C.rmsnorm_fixed_order(xs, rs, w, 1e-5, dt)
+            ok = ok and bool(np.array_equal(y, ym) and np.array_equal(ro, rom))
     else:
         y = host(wl.fn()[sel])
-        ym = C.rmsnorm_fixed_order(xs, None, w, 1e-6, dt)
         yo = C.rmsnorm(xs, w, 1e-6, dt)
-        ok = bool(np.array_equal(y, ym))
+        if vectors:
+            ok = bool(np.array_equal(y, C.rmsnorm_fixed_order(xs, None, w, 1e-6, dt)))
     worst = int(O.ulp_distance(yo, y, dt).max())
     ok = ok and worst <= (2 if dt != O.F32 else 6)
     return {"ok": ok, "rows": [wl.lo + i for i in sel], "max_ulp_vs_reference_order": worst}
