@@ -174,7 +174,7 @@ struct SwigluPlan {
 // threads.
 constexpr int kThreadsPerSm = 2048;
 
-SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat) {
+SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat, bool bf16) {
     if (vector_ok && g_threads == 0 && rows * h <= kTinyElements) {
         // Decode-sized problems are latency-bound: two elements per thread
         // (4-byte accesses) spread them over four times the threads, which
@@ -201,15 +201,17 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // bf16 and fp16; e.g. bf16 16384 x 14336 packed 224.9 -> 218.5 us).
         // The strided kernel with two vectors takes 48 registers, so a full
         // SM's budget of 256-thread CTAs leaves 5 resident and the rest to a
-        // second, uneven pass; with 1024 threads all are resident. Dense
-        // operands keep two vectors and the full budget (59 registers: 4
-        // resident CTAs, two even passes), measured equal or faster.
+        // second, uneven pass; with 1024 threads all are resident. fp16 dense
+        // operands gain the same way (1.5-2% at F 11008 and 14336); bf16
+        // dense operands measured 1.5-2% faster with the full budget (59
+        // registers: 4 resident CTAs, two even passes).
         const int64_t total = rows * (h * es / 16);
         const bool small = total < static_cast<int64_t>(sm_count()) * kThreads * 4;
         const bool huge = total >= (int64_t{1} << 24);
+        const bool full_budget = !huge || (flat && bf16);
         return SwigluPlan{16, g_threads > 0 ? g_threads : (small ? 128 : kThreads),
                           g_unroll > 0 ? g_unroll : (huge ? 2 : 1),
-                          g_threads_per_sm > 0 ? g_threads_per_sm : (huge && !flat ? 1024 : kThreadsPerSm)};
+                          g_threads_per_sm > 0 ? g_threads_per_sm : (full_budget ? kThreadsPerSm : 1024)};
     }
     return SwigluPlan{es, 256, 4, kThreadsPerSm};
 }
@@ -231,7 +233,8 @@ int launch_vec(const SwigluArgs& a, bool flat, const SwigluPlan& p, cudaStream_t
 template <typename T>
 int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaStream_t st) {
     constexpr int VEC = 16 / sizeof(T);
-    const SwigluPlan p = swiglu_plan(rows, h, static_cast<int>(sizeof(T)), vector_ok, flat);
+    const SwigluPlan p = swiglu_plan(rows, h, static_cast<int>(sizeof(T)), vector_ok, flat,
+                                     std::is_same_v<T, __nv_bfloat16>);
     const int per_access = p.access_bytes / static_cast<int>(sizeof(T));
     a.per_row = h / per_access;
     a.total = rows * a.per_row;
@@ -286,7 +289,7 @@ extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtyp
     if (n_rows < 1 || hidden_dim < 1)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_swiglu_plan: empty problem");
     const bool vector_ok = aligned != 0 && (hidden_dim * es) % 16 == 0;
-    const SwigluPlan p = swiglu_plan(n_rows, hidden_dim, es, vector_ok, dense != 0);
+    const SwigluPlan p = swiglu_plan(n_rows, hidden_dim, es, vector_ok, dense != 0, dtype == AKO_B200_BF16);
     *access_bytes = p.access_bytes;
     *threads = p.threads;
     *vectors_per_thread = p.unroll;

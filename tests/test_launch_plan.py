@@ -140,6 +140,7 @@ def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool
         (16384, 14336, BF16, True, True, (16, 256, 2, 2048)),   # 2^24.8 dense vectors: two per thread
         (16384, 14336, BF16, True, False, (16, 256, 2, 1024)),  # packed halves (strided): two, 1024 threads/SM
         (16384, 11008, F16, True, False, (16, 256, 2, 1024)),
+        (16384, 14336, F16, True, True, (16, 256, 2, 1024)),    # fp16 dense: the same budget
         (16384, 5632, BF16, True, False, (16, 256, 1, 2048)),   # below 2^24 vectors
         (2048, 11008, F16, True, True, (16, 256, 1, 2048)),
         (64, 14336, BF16, True, True, (16, 128, 1, 2048)),      # decode rows: 128-thread CTAs
