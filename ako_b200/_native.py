@@ -77,6 +77,7 @@ MEASURE_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ako_b200_rope_set_launch": (_c_int, [_c_int]),
     "ako_b200_swiglu_set_launch": (_c_int, [_c_int, _c_int]),
     "ako_b200_swiglu_set_grid": (_c_int, [_c_int]),
+    "ako_b200_swiglu_set_smem": (_c_int, [_c_int]),
     "ako_b200_set_pdl": (_c_int, [_c_int]),
 }
 

@@ -48,6 +48,9 @@ constexpr int64_t kTinyElements = int64_t{1} << 15;  // up to this many: 4-byte 
 AKO_B200_OVERRIDE int g_threads = 0;
 AKO_B200_OVERRIDE int g_unroll = 0;
 AKO_B200_OVERRIDE int g_threads_per_sm = 0;
+// Dynamic shared memory per CTA (unused by the kernel): limits how many CTAs
+// an SM holds at once. Measurement builds only.
+AKO_B200_OVERRIDE int g_smem_bytes = 0;
 
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
@@ -145,22 +148,31 @@ __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
     }
 }
 
+// Dynamic shared memory (unused by the kernel) that leaves room for at most
+// four CTAs on an SM: 5 x (48 KB + the 1 KB the runtime reserves per CTA)
+// exceeds an SM's 228 KB, 4 x 49 KB does not.
+constexpr int kFourResidentSmem = 48 * 1024;
+
 // The grid strides over the vectors with at most `threads_per_sm` threads
-// per SM (CTAs of THREADS threads).
+// per SM (CTAs of THREADS threads); with `four_resident`, at most four CTAs
+// of it are on an SM at once (the rest run as those finish).
 template <typename T, int VEC, int UNROLL, int THREADS>
-int launch(SwigluArgs a, bool flat, int threads_per_sm, cudaStream_t st) {
+int launch(SwigluArgs a, bool flat, int threads_per_sm, bool four_resident, cudaStream_t st) {
     const int64_t per_cta = static_cast<int64_t>(THREADS) * UNROLL;
     int64_t grid = (a.total + per_cta - 1) / per_cta;
     const int ctas_per_sm = threads_per_sm >= THREADS ? threads_per_sm / THREADS : 1;
     const int64_t cap = static_cast<int64_t>(sm_count()) * ctas_per_sm;
     if (grid > cap) grid = cap;
     const dim3 g(static_cast<unsigned>(grid));
-    if (flat) return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
+    const int smem = g_smem_bytes > 0 ? g_smem_bytes : four_resident ? kFourResidentSmem : 0;
+    if (flat)
+        return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
     if (a.total <= static_cast<int64_t>(UINT_MAX)) {
         a.row_div = FastDiv::make(static_cast<uint32_t>(a.per_row));
-        return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, true, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
+        return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, true, THREADS>, g, dim3(THREADS), smem, 1, st, a,
+                         "swiglu");
     }
-    return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS>, g, dim3(THREADS), 0, 1, st, a, "swiglu");
+    return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
 }
 
 // Launch choice for a call: bytes per access (16, 4 for decode-sized
@@ -168,13 +180,14 @@ int launch(SwigluArgs a, bool flat, int threads_per_sm, cudaStream_t st) {
 // CTA size and vectors per thread.
 struct SwigluPlan {
     int access_bytes, threads, unroll, threads_per_sm;
+    bool four_resident;
 };
 
 // Thread budget per SM of the grid-stride grid, built-in: a full SM of
 // threads.
 constexpr int kThreadsPerSm = 2048;
 
-SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat, bool bf16) {
+SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool flat) {
     if (vector_ok && g_threads == 0 && rows * h <= kTinyElements) {
         // Decode-sized problems are latency-bound: two elements per thread
         // (4-byte accesses) spread them over four times the threads, which
@@ -182,7 +195,7 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // reciprocals. In CUDA graphs on B200 this is 0.1 us faster per call
         // for fp16 and fp32 rows of 5632-14336 at 1-2 rows and the same for
         // bf16; above 2^15 elements 16-byte accesses are as fast or faster.
-        return SwigluPlan{4, 128, 1, kThreadsPerSm};
+        return SwigluPlan{4, 128, 1, kThreadsPerSm, false};
     }
     if (vector_ok) {
         // 256-thread CTAs with one vector of each input per thread (32
@@ -194,52 +207,51 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // few vectors spread over many SMs (measured fastest up to ~64 rows of
         // 5632..14336).
         //
-        // Strided operands (the packed [M, 2F] halves) of 2^24 vectors and more
-        // stream fastest with two vectors per thread and at most 1024 threads
-        // per SM: 2-3% faster than one vector and a full SM of threads on
-        // every such cell measured on B200 (F 11008 and 14336, 16384 rows,
-        // bf16 and fp16; e.g. bf16 16384 x 14336 packed 224.9 -> 218.5 us).
-        // The strided kernel with two vectors takes 48 registers, so a full
-        // SM's budget of 256-thread CTAs leaves 5 resident and the rest to a
-        // second, uneven pass; with 1024 threads all are resident. fp16 dense
-        // operands gain the same way (1.5-2% at F 11008 and 14336); bf16
-        // dense operands measured 1.5-2% faster with the full budget (59
-        // registers: 4 resident CTAs, two even passes).
+        // Problems of 2^24 vectors and more stream fastest with two vectors
+        // per thread. Dense operands then want a full SM's budget of 256-thread
+        // CTAs with at most four of them resident (two even passes): measured
+        // on B200 at 16384 x 11008 and x 14336, fp16 1-2% faster than one pass
+        // of four (218.2 -> 213.5 us at F 14336) and 3-4% faster than five or
+        // more resident, bf16 (59 registers: four resident anyway) unchanged.
+        // Strided operands (the packed [M, 2F] halves) want one pass of four
+        // (1024 threads per SM): 2-3% faster than a full SM of one-vector
+        // threads (bf16 16384 x 14336 packed 224.9 -> 218.5 us), and level
+        // with two passes of four.
         const int64_t total = rows * (h * es / 16);
         const bool small = total < static_cast<int64_t>(sm_count()) * kThreads * 4;
         const bool huge = total >= (int64_t{1} << 24);
-        const bool full_budget = !huge || (flat && bf16);
         return SwigluPlan{16, g_threads > 0 ? g_threads : (small ? 128 : kThreads),
                           g_unroll > 0 ? g_unroll : (huge ? 2 : 1),
-                          g_threads_per_sm > 0 ? g_threads_per_sm : (full_budget ? kThreadsPerSm : 1024)};
+                          g_threads_per_sm > 0 ? g_threads_per_sm : (huge && !flat ? 1024 : kThreadsPerSm),
+                          huge && flat && g_threads == 0 && g_threads_per_sm == 0};
     }
-    return SwigluPlan{es, 256, 4, kThreadsPerSm};
+    return SwigluPlan{es, 256, 4, kThreadsPerSm, false};
 }
 
 template <typename T, int VEC>
 int launch_vec(const SwigluArgs& a, bool flat, const SwigluPlan& p, cudaStream_t st) {
     const int tps = p.threads_per_sm;
+    const bool four = p.four_resident;
     switch (p.threads * 16 + p.unroll) {
-        case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, tps, st);
-        case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, tps, st);
-        case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, tps, st);
-        case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, tps, st);
-        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, tps, st);
-        case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, tps, st);
-        default: return launch<T, VEC, 2, 256>(a, flat, tps, st);
+        case 64 * 16 + 1: return launch<T, VEC, 1, 64>(a, flat, tps, four, st);
+        case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, tps, four, st);
+        case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, tps, four, st);
+        case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, tps, four, st);
+        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, tps, four, st);
+        case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, tps, four, st);
+        default: return launch<T, VEC, 2, 256>(a, flat, tps, four, st);
     }
 }
 
 template <typename T>
 int run(SwigluArgs a, int64_t rows, int64_t h, bool vector_ok, bool flat, cudaStream_t st) {
     constexpr int VEC = 16 / sizeof(T);
-    const SwigluPlan p = swiglu_plan(rows, h, static_cast<int>(sizeof(T)), vector_ok, flat,
-                                     std::is_same_v<T, __nv_bfloat16>);
+    const SwigluPlan p = swiglu_plan(rows, h, static_cast<int>(sizeof(T)), vector_ok, flat);
     const int per_access = p.access_bytes / static_cast<int>(sizeof(T));
     a.per_row = h / per_access;
     a.total = rows * a.per_row;
-    if (!vector_ok) return launch<T, 1, 4, 256>(a, flat, p.threads_per_sm, st);
-    if (p.access_bytes == 4) return launch<T, 4 / sizeof(T), 1, 128>(a, flat, p.threads_per_sm, st);
+    if (!vector_ok) return launch<T, 1, 4, 256>(a, flat, p.threads_per_sm, false, st);
+    if (p.access_bytes == 4) return launch<T, 4 / sizeof(T), 1, 128>(a, flat, p.threads_per_sm, false, st);
     return launch_vec<T, VEC>(a, flat, p, st);
 }
 
@@ -289,7 +301,7 @@ extern "C" int ako_b200_swiglu_plan(int64_t n_rows, int64_t hidden_dim, int dtyp
     if (n_rows < 1 || hidden_dim < 1)
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "ako_b200_swiglu_plan: empty problem");
     const bool vector_ok = aligned != 0 && (hidden_dim * es) % 16 == 0;
-    const SwigluPlan p = swiglu_plan(n_rows, hidden_dim, es, vector_ok, dense != 0, dtype == AKO_B200_BF16);
+    const SwigluPlan p = swiglu_plan(n_rows, hidden_dim, es, vector_ok, dense != 0);
     *access_bytes = p.access_bytes;
     *threads = p.threads;
     *vectors_per_thread = p.unroll;
@@ -313,10 +325,18 @@ extern "C" int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread) {
 
 extern "C" int ako_b200_swiglu_set_grid(int threads_per_sm) {
     clear_error();
-    if (threads_per_sm != 0 && (threads_per_sm < 64 || threads_per_sm > 2048 || threads_per_sm % 64 != 0))
+    if (threads_per_sm != 0 && (threads_per_sm < 64 || threads_per_sm > 8192 || threads_per_sm % 64 != 0))
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT,
-                         "swiglu grid budget must be 0 or a multiple of 64 in [64, 2048], got %d", threads_per_sm);
+                         "swiglu grid budget must be 0 or a multiple of 64 in [64, 8192], got %d", threads_per_sm);
     g_threads_per_sm = threads_per_sm;
+    return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_swiglu_set_smem(int bytes) {
+    clear_error();
+    if (bytes < 0 || bytes > 48 * 1024)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "swiglu shared memory must be in [0, 49152], got %d", bytes);
+    g_smem_bytes = bytes;
     return AKO_B200_OK;
 }
 #endif  // AKO_B200_MEASUREMENT

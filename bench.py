@@ -134,6 +134,20 @@ def global_rows(lo: int, hi: int, hidden: int, dtype: torch.dtype, device, seed:
     return x, r
 
 
+def global_blocks(lo: int, hi: int, shape: tuple[int, ...], dtype: torch.dtype, device, seed: int, std: float,
+                  per_block: int) -> torch.Tensor:
+    """Entries ``[lo, hi)`` along the first axis of a seeded N(0, std) tensor
+    of entries ``shape``, drawn ``per_block`` entries per seed, so a shard's
+    bytes do not depend on how the batch is split."""
+    out = torch.empty(hi - lo, *shape, dtype=dtype, device=device)
+    for b in range(lo // per_block, (hi + per_block - 1) // per_block):
+        g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 500_000 + b)
+        blk = (torch.randn(per_block, *shape, generator=g, device=device) * std).to(dtype)
+        a, z = max(lo, b * per_block), min(hi, (b + 1) * per_block)
+        out[a - lo:z - lo] = blk[a - b * per_block:z - b * per_block]
+    return out
+
+
 def weight(hidden: int, dtype: torch.dtype, device, seed: int) -> torch.Tensor:
     """The workload's weight, N(1, 0.1), from a seed no row block uses."""
     g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 1_000_000)
@@ -143,8 +157,8 @@ def weight(hidden: int, dtype: torch.dtype, device, seed: int) -> torch.Tensor:
 class Workload:
     """Inputs in HBM, one kernel launch per step, and its algorithmic bytes.
 
-    Row ops hold rows ``[lo, hi)`` of the workload's seeded global batch; the
-    other ops hold the whole cell.
+    Each op holds entries ``[lo, hi)`` along the first axis of its seeded
+    global batch (rows; the batch for RoPE), the whole batch by default.
     """
 
     def __init__(self, name: str, device: torch.device, seed: int = 0, rows: tuple[int, int] | None = None) -> None:
@@ -154,10 +168,10 @@ class Workload:
         self.op, self.dims, self.dtype = WORKLOADS[name]
         b = torch.tensor([], dtype=self.dtype).element_size()
         self.element_size = b
+        self.lo, self.hi = rows or (0, self.dims[0])
+        n = self.hi - self.lo
         if self.op in ("rmsnorm", "rmsnorm_residual"):
-            m, h = self.dims
-            self.lo, self.hi = rows or (0, m)
-            n = self.hi - self.lo
+            h = self.dims[1]
             self.x, r = global_rows(self.lo, self.hi, h, self.dtype, device, seed)
             self.w = weight(h, self.dtype, device, seed)
             if self.op == "rmsnorm":
@@ -171,38 +185,38 @@ class Workload:
             self.desc = {"rows": n, "hidden": h}
             self.kernel = "ako_b200::rms_rows_kernel"
             return
-        g = torch.Generator(device=device).manual_seed(seed)
-        rnd = lambda *s, mean=0.0, std=1.0: (torch.randn(*s, generator=g, device=device) * std + mean).to(self.dtype)  # noqa: E731
         if self.op in ("rope", "rope_qk"):
-            bb, s, hh, d = self.dims
+            _, s, hh, d = self.dims
             from ako_b200.api import build_rope_tables
 
             cos, sin = build_rope_tables(8192, d, device=device)
             self.cos, self.sin = cos[:s], sin[:s]
-            self.x = rnd(bb, s, hh, d)
+            # one batch entry per seed: q from one seed range, k from another
+            self.x = global_blocks(self.lo, self.hi, (s, hh, d), self.dtype, device, seed, 1.0, 1)
             table = s * (d // 2) * 4 * 2
             if self.op == "rope":
-                self.bytes = 2 * bb * s * hh * d * b + table
+                self.bytes = 2 * n * s * hh * d * b + table
                 self.fn = lambda: kernels.rope_cuda_sm100(self.x, self.cos, self.sin, "neox")
-                self.desc = {"batch": bb, "seq": s, "heads": hh, "head_dim": d, "style": "neox",
+                self.desc = {"batch": n, "seq": s, "heads": hh, "head_dim": d, "style": "neox",
                              "table": "fp32 [8192, 64] sliced"}
             else:
-                self.k = rnd(bb, s, 8, d)
-                self.bytes = 2 * bb * s * (hh + 8) * d * b + table
+                self.k = global_blocks(self.lo, self.hi, (s, 8, d), self.dtype, device, seed + 7, 1.0, 1)
+                self.bytes = 2 * n * s * (hh + 8) * d * b + table
                 self.fn = lambda: kernels.rope_qk_cuda_sm100(self.x, self.k, self.cos, self.sin, "neox")
-                self.desc = {"batch": bb, "seq": s, "q_heads": hh, "k_heads": 8, "head_dim": d, "style": "neox",
+                self.desc = {"batch": n, "seq": s, "q_heads": hh, "k_heads": 8, "head_dim": d, "style": "neox",
                              "table": "fp32 [8192, 64] sliced, read once for q and k"}
             self.kernel = "ako_b200::rope_vec_kernel"
             return
-        m, f = self.dims
+        f = self.dims[1]
         if self.op == "swiglu_packed":
-            self.packed = rnd(m, 2 * f, std=2.0)
+            self.packed = global_blocks(self.lo, self.hi, (2 * f,), self.dtype, device, seed, 2.0, ROW_BLOCK)
             self.g, self.u = self.packed[:, :f], self.packed[:, f:]
         else:
-            self.g, self.u = rnd(m, f, std=2.0), rnd(m, f, std=2.0)
-        self.bytes = 3 * m * f * b
+            self.g = global_blocks(self.lo, self.hi, (f,), self.dtype, device, seed, 2.0, ROW_BLOCK)
+            self.u = global_blocks(self.lo, self.hi, (f,), self.dtype, device, seed + 7, 2.0, ROW_BLOCK)
+        self.bytes = 3 * n * f * b
         self.fn = lambda: kernels.swiglu_cuda_sm100(self.g, self.u)
-        self.desc = {"rows": m, "hidden": f, "packed": self.op == "swiglu_packed"}
+        self.desc = {"rows": n, "hidden": f, "packed": self.op == "swiglu_packed"}
         self.kernel = "ako_b200::swiglu_kernel"
 
     def step(self) -> None:
@@ -278,9 +292,11 @@ def ncu_traffic(workload: str) -> int | None:
 
 # ------------------------------------------------------------------ parity
 def shard_parity(wl: Workload) -> dict:
-    """Rows of this rank's shard (its first, middle and last) against the C
-    model of the kernels' fixed summation order (bit for bit) and the
-    reference-order oracle (AKO's gate), on the host."""
+    """This rank's shard on the host against the C oracle: three of its rows
+    (its first, middle and last; for RoPE, those batch entries). RMSNorm rows
+    are held to the C model of the kernels' fixed summation order bit for bit
+    and to the reference-order oracle within AKO's ulp bound; RoPE is
+    bit-exact; SwiGLU is within 2 ulp (16-bit) of the reference's formula."""
     import numpy as np
 
     from oracle import ako_oracle as O
@@ -288,13 +304,26 @@ def shard_parity(wl: Workload) -> dict:
 
     def host(t: torch.Tensor) -> np.ndarray:
         t = t.detach().cpu().contiguous()
-        return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+        return t.view(torch.int16).numpy().view(np.uint16) if t.dtype in (torch.bfloat16, torch.float16) else t.numpy()
 
     n = wl.hi - wl.lo
     sel = sorted({0, n // 2, n - 1})
     dt = {torch.bfloat16: O.BF16, torch.float16: O.F16, torch.float32: O.F32}[wl.dtype]
-    xs, w = host(wl.x[sel]), host(wl.w)
     ok, worst = True, 0
+    if wl.op in ("rope", "rope_qk"):
+        cos, sin = wl.cos.cpu().numpy(), wl.sin.cpu().numpy()
+        outs = wl.fn()
+        pairs = [(wl.x, outs)] if wl.op == "rope" else [(wl.x, outs[0]), (wl.k, outs[1])]
+        for src, out in pairs:
+            d = O.ulp_distance(C.rope(host(src[sel]), cos, sin, "neox", dt), host(out[sel]), dt)
+            worst = max(worst, int(d.max()))
+        return {"ok": worst == 0, "batch_entries": [wl.lo + i for i in sel], "max_ulp_vs_reference": worst}
+    if wl.op in ("swiglu", "swiglu_packed"):
+        y = host(wl.fn()[sel])
+        worst = int(O.ulp_distance(C.swiglu(host(wl.g[sel]), host(wl.u[sel]), dt), y, dt).max())
+        return {"ok": worst <= (2 if dt != O.F32 else 6), "rows": [wl.lo + i for i in sel],
+                "max_ulp_vs_reference": worst}
+    xs, w = host(wl.x[sel]), host(wl.w)
     # rows of whole 16-byte vectors run on the vector kernels, held to the fixed-order model
     vectors = (xs.shape[-1] * xs.dtype.itemsize) % 16 == 0
     if wl.op == "rmsnorm_residual":
@@ -353,6 +382,9 @@ def ako_reference_cpu(rows: int, hidden: int, dtype: torch.dtype, warmup: int, r
     from ako.benchmark.bench_op import bench_op
     from ako.ops.rmsnorm_ref import rmsnorm_residual_ref
 
+    # All the host threads this process may run on (a launcher such as
+    # torchrun sets OMP_NUM_THREADS=1 for its ranks).
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     x, r = global_rows(0, rows, hidden, dtype, "cpu", 0)
     w = weight(hidden, dtype, "cpu", 0)
     res = bench_op(rmsnorm_residual_ref, (x, r, w), call_kwargs={"eps": 1e-5}, warmup=warmup, repeats=repeats,
@@ -365,7 +397,6 @@ def ako_reference_cpu(rows: int, hidden: int, dtype: torch.dtype, warmup: int, r
                       f"ako.ops.rmsnorm_ref.rmsnorm_residual_ref on CPU tensors, timed by ako.benchmark.bench_op "
                       f"(warmup {warmup}, {repeats} timed calls, p50 {res.latency_p50_ms:.1f} ms)",
             "ms_per_call": round(res.latency_p50_ms, 3), "bytes_per_call": nbytes, **cpu_description()}
-
 
 
 def c_port_cpu(rows: int, hidden: int, dtype: torch.dtype, seconds: float) -> dict:
@@ -519,7 +550,7 @@ def main() -> None:
     peak, peak_src = hbm_peak()
     op, dims, _ = WORKLOADS[args.workload]
     row_op = op in ("rmsnorm", "rmsnorm_residual")
-    strong = args.scaling == "strong" and row_op
+    strong = args.scaling == "strong"
     shard = sharding.shard_range(dims[0], world, rank) if strong else None
 
     wl = Workload(args.workload, device, seed=0, rows=shard)
@@ -531,17 +562,17 @@ def main() -> None:
     step_bytes = sharding.sum_over_ranks(wl.bytes, device)  # the global batch (strong) or N batches (weak)
     value = step_bytes / (per_step_ms * 1e-3) / 1e9
     achieved = wl.bytes / ((ms / args.steps) * 1e-3) / 1e9  # this rank's kernel
-    parity = shard_parity(wl) if row_op else None
-    parity_all = sharding.all_over_ranks(parity["ok"], device) if parity is not None else None
+    parity = shard_parity(wl)
+    parity_all = sharding.all_over_ranks(parity["ok"], device)
 
     weak = None
     if world > 1 and strong:
-        full = Workload(args.workload, device, seed=rank + 1)
+        full = Workload(args.workload, device, seed=100 + rank)
         wms = timed_region(full.step, args.steps, args.warmup)
         wmax = sharding.max_over_ranks(wms, device)
         weak = {"value": round(full.bytes * world / (wmax / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(wmax / args.steps, 4),
-                "config": f"a whole {dims[0]}-row batch on every rank ({world} batches per step)"}
+                "config": f"a whole batch on every rank ({world} batches per step)"}
         del full
         torch.cuda.empty_cache()
 
@@ -606,15 +637,17 @@ def main() -> None:
         "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if wl.dtype == torch.bfloat16 else str(wl.dtype).replace("torch.", ""),
-        "data": "synthetic (seeded N(0,1) rows, weight N(1,0.1), generated on device by global row index)",
+        "data": "synthetic (seeded N(0,1) rows, weight N(1,0.1); N(0,2) SwiGLU inputs; generated on device by global row or batch index)",
         "config": {
             "workload": args.workload,
             "op": wl.op,
-            **({"global_rows": dims[0], "rows_per_gpu": wl.hi - wl.lo, "hidden": dims[1]} if row_op else wl.desc),
+            **({"global_rows": dims[0], "rows_per_gpu": wl.hi - wl.lo, "hidden": dims[1]} if row_op else
+               {**wl.desc, ("global_batch" if op.startswith("rope") else "global_rows"): dims[0]}),
             "bytes_per_step": step_bytes,
             "l2": "inputs larger than L2 (the step moves far more than the 126 MB L2); no flush",
-            "parallelism": (f"one {dims[0]}-row batch split into {world} contiguous row blocks "
-                            f"(ako_b200.sharding.shard_range), no collective on the data path" if strong else
+            "parallelism": (f"one {dims[0]}-{'entry' if op.startswith('rope') else 'row'} batch split into {world} "
+                            f"contiguous blocks (ako_b200.sharding.shard_range), no collective on the data path"
+                            if strong else
                             f"a whole batch per rank x{world}, no collective on the data path"),
         },
         "roofline": {

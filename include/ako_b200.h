@@ -232,8 +232,9 @@ int ako_b200_rope_plan(int64_t batch, int64_t seq_len, int64_t n_heads, int64_t 
  * without launching anything (host only; no GPU needed): bytes per access
  * (16; 4 for decode-sized problems; the element size when the operands are
  * not 16-byte aligned), threads per CTA, vectors per thread, and the grid's
- * budget of threads per SM (the grid strides over the problem with at most
- * that many threads on each SM). `aligned`
+ * budget of threads per SM (the grid strides over the problem with that many
+ * threads for each SM; dense problems of 2^24 or more vectors keep at most
+ * four CTAs on an SM at once and run the rest as those finish). `aligned`
  * says whether the call's pointers and row strides are 16-byte aligned,
  * `dense` whether all three operands are contiguous. Follows the library's
  * built-in choice (in the measurement build, any override in force). Not

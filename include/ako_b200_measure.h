@@ -65,11 +65,18 @@ int ako_b200_rope_set_launch(int heads_per_thread);
 int ako_b200_swiglu_set_launch(int threads, int vectors_per_thread);
 
 /*
- * SwiGLU grid budget: the grid-stride grid keeps at most `threads_per_sm`
- * threads on each SM (a multiple of 64 in [64, 2048]); 0 restores the
- * built-in choice.
+ * SwiGLU grid budget: the grid-stride grid has at most `threads_per_sm`
+ * threads for each SM (a multiple of 64 in [64, 8192]; above what an SM holds
+ * at once, the CTAs run in several passes); 0 restores the built-in choice.
  */
 int ako_b200_swiglu_set_grid(int threads_per_sm);
+
+/*
+ * SwiGLU CTAs request `bytes` of dynamic shared memory (in [0, 49152]), which
+ * the kernel does not use: it caps how many CTAs an SM holds at once. 0
+ * restores the built-in launch.
+ */
+int ako_b200_swiglu_set_smem(int bytes);
 
 /*
  * Programmatic dependent launch: with `enable` = 1 (the built-in setting)

@@ -11,6 +11,7 @@ import subprocess
 import sys
 from pathlib import Path
 
+import pytest
 import torch
 
 from ako_b200.benchmark.sweep import cell_label, report
@@ -143,6 +144,25 @@ def test_shards_of_the_global_batch_are_its_rows() -> None:
     assert not torch.equal(whole_x[:1024], whole_r[:1024])
     w = bench.weight(h, torch.float32, "cpu", 0)
     assert abs(w.mean().item() - 1.0) < 0.1
+
+
+@pytest.mark.parametrize("shape, per_block, std", [((24,), 1024, 2.0), ((3, 2, 8), 1, 1.0)],
+                         ids=["swiglu-rows", "rope-batch"])
+def test_shards_of_other_ops_are_their_batch(shape, per_block, std) -> None:
+    """SwiGLU rows and RoPE batch entries are drawn per block of the first
+    axis, so every GPU count's shards concatenate to the one-GPU tensor."""
+    import bench
+    from ako_b200.sharding import shard_range
+
+    m = 2500 if per_block > 1 else 11
+    whole = bench.global_blocks(0, m, shape, torch.bfloat16, "cpu", 0, std, per_block)
+    for world in (2, 3, 8):
+        parts = [bench.global_blocks(*shard_range(m, world, r), shape, torch.bfloat16, "cpu", 0, std, per_block)
+                 for r in range(world)]
+        assert torch.equal(torch.cat(parts), whole)
+    assert abs(whole.float().std().item() - std) < 0.1 * std
+    other = bench.global_blocks(0, m, shape, torch.bfloat16, "cpu", 7, std, per_block)
+    assert not torch.equal(other, whole)
 
 
 def test_host_rows_that_fit_is_bounded() -> None:

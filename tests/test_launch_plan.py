@@ -39,13 +39,14 @@ def _built_in_choice():
     m = _native.measure_lib()
     for f in (lambda: m.ako_b200_rmsnorm_set_launch(0, 0, 0), lambda: m.ako_b200_rmsnorm_set_staging(0, 0, 0),
               lambda: m.ako_b200_swiglu_set_launch(0, 0), lambda: m.ako_b200_rope_set_launch(0),
-              lambda: m.ako_b200_swiglu_set_grid(0)):
+              lambda: m.ako_b200_swiglu_set_grid(0), lambda: m.ako_b200_swiglu_set_smem(0)):
         f()
     yield
     m.ako_b200_rmsnorm_set_launch(0, 0, 0)
     m.ako_b200_rmsnorm_set_staging(0, 0, 0)
     m.ako_b200_swiglu_set_launch(0, 0)
     m.ako_b200_swiglu_set_grid(0)
+    m.ako_b200_swiglu_set_smem(0)
     m.ako_b200_rope_set_launch(0)
 
 
@@ -140,7 +141,7 @@ def swiglu_plan(rows: int, f: int, dtype: int, aligned: bool = True, dense: bool
         (16384, 14336, BF16, True, True, (16, 256, 2, 2048)),   # 2^24.8 dense vectors: two per thread
         (16384, 14336, BF16, True, False, (16, 256, 2, 1024)),  # packed halves (strided): two, 1024 threads/SM
         (16384, 11008, F16, True, False, (16, 256, 2, 1024)),
-        (16384, 14336, F16, True, True, (16, 256, 2, 1024)),    # fp16 dense: the same budget
+        (16384, 14336, F16, True, True, (16, 256, 2, 2048)),    # fp16 dense: a full budget, four resident
         (16384, 5632, BF16, True, False, (16, 256, 1, 2048)),   # below 2^24 vectors
         (2048, 11008, F16, True, True, (16, 256, 1, 2048)),
         (64, 14336, BF16, True, True, (16, 128, 1, 2048)),      # decode rows: 128-thread CTAs
@@ -162,7 +163,12 @@ def test_swiglu_override_is_followed() -> None:
     assert swiglu_plan(1, 5632, BF16, lib=m) == (16, 64, 2, 2048)  # an override also skips the decode-sized path
     assert m.ako_b200_swiglu_set_grid(1536) == 0
     assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2, 1536)
-    assert m.ako_b200_swiglu_set_grid(100) == 1 and m.ako_b200_swiglu_set_grid(0) == 0
+    assert m.ako_b200_swiglu_set_grid(4096) == 0
+    assert swiglu_plan(2048, 11008, BF16, lib=m) == (16, 64, 2, 4096)
+    assert m.ako_b200_swiglu_set_grid(100) == 1 and m.ako_b200_swiglu_set_grid(8256) == 1
+    assert m.ako_b200_swiglu_set_grid(0) == 0
+    assert m.ako_b200_swiglu_set_smem(48 * 1024) == 0 and m.ako_b200_swiglu_set_smem(48 * 1024 + 1) == 1
+    assert m.ako_b200_swiglu_set_smem(-1) == 1 and m.ako_b200_swiglu_set_smem(0) == 0
     assert swiglu_plan(2048, 11008, BF16) == (16, 256, 1, 2048)
 
 
