@@ -359,8 +359,11 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
     const int nvec = (a.h - head) / VEC;
     const int tail = head + nvec * VEC;
 
-    // Rounded squares accumulated in fp64 per thread (any row length stays
-    // within one fp32 rounding of the exact sum), then pairwise across threads.
+    // Rounded squares: each 16-byte vector's summed pairwise in fp32, those
+    // sums and the ends' squares accumulated in fp64 per thread (any row
+    // length stays within a few fp32 roundings of the exact sum), then
+    // pairwise across threads. One conversion and one fp64 add per vector:
+    // per element they made the kernel issue-bound.
     double acc = 0.0;
     auto first_pass = [&](int col) {
         float f = to_f32(xr[col]);
@@ -386,12 +389,14 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
             }
             st_global<T, VEC>(ro + col, xv);
         }
+        float sq[VEC];
 #pragma unroll
         for (int e = 0; e < VEC; e += 2) {
             const float2 f = get2<T, VEC>(xv, e);
-            acc += static_cast<double>(__fmul_rn(f.x, f.x));
-            acc += static_cast<double>(__fmul_rn(f.y, f.y));
+            sq[e] = __fmul_rn(f.x, f.x);
+            sq[e + 1] = __fmul_rn(f.y, f.y);
         }
+        acc += static_cast<double>(tree_sum<VEC>(sq));
     }
     const float total = block_sum<kGenericThreads>(static_cast<float>(acc), scratch);
     const float inv = rms_inv(total, a);
