@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 MEASURE_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ako_b200_rmsnorm_set_launch": (_c_int, [_c_int, _c_int, _c_int]),
     "ako_b200_rmsnorm_set_staging": (_c_int, [_c_int, _c_int, _c_int]),
+    "ako_b200_rmsnorm_set_generic": (_c_int, [_c_int]),
     "ako_b200_measure_set_wait_polls": (ctypes.c_uint, [ctypes.c_uint]),
     "ako_b200_rope_set_launch": (_c_int, [_c_int]),
     "ako_b200_swiglu_set_launch": (_c_int, [_c_int, _c_int]),

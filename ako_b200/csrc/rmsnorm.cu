@@ -26,6 +26,28 @@ AKO_B200_OVERRIDE int g_ctas_per_sm = 0;
 // builds can lower it to exercise the expiry path).
 AKO_B200_OVERRIDE uint32_t g_wait_polls = kWaitPolls;
 
+// Any-width kernel: threads per row (0: the built-in choice below; 32 or 256
+// forced). Measurement builds only.
+AKO_B200_OVERRIDE int g_generic_tpr = 0;
+
+// Rows of at most this many bytes take the any-width kernel with a warp per
+// row (four rows per CTA); wider rows take a 256-thread CTA per row. The
+// choice depends on the width alone, so a row's bits do not depend on the
+// batch. Measured on B200 (cold L2, 2048-65536 rows): a CTA per row idles
+// most of its threads on narrow rows (bf16 1001 wide: 0.25 of peak plain and
+// 0.43 fused, against 0.55 and 0.75 with a warp; fp32 517: 0.28 -> 0.70); a
+// warp per row is ahead up to 8200-byte plain rows (bf16 4100: 0.69 -> 0.73,
+// fp32 2049: 0.64 -> 0.78) and 6000-byte fused ones (bf16 3001: 0.74 ->
+// 0.80), and behind above (fused bf16 4100: 0.93 -> 0.76).
+constexpr int64_t kGenericWarpMaxBytesPlain = 8704;
+constexpr int64_t kGenericWarpMaxBytesFused = 6144;
+
+int generic_tpr(const RmsArgs& a, int es, bool res) {
+    if (g_generic_tpr != 0) return g_generic_tpr;
+    const int64_t row_bytes = static_cast<int64_t>(a.h) * es;
+    return row_bytes <= (res ? kGenericWarpMaxBytesFused : kGenericWarpMaxBytesPlain) ? 32 : kGenericThreads;
+}
+
 // Rows from which plain 16-bit rows of 2049-4096 vectors take the staged kernel.
 constexpr int64_t kStagedMinRows = 1024;
 // Rows from which plain 16-bit rows of 4097-8192 vectors take the chunked
@@ -202,7 +224,7 @@ Plan plan_for(const RmsArgs& a, int dtype, bool res, bool vector_ok) {
         Shape s;
         if (pick_shape(a.h / (16 / es), a.rows, res, es, &s)) return Plan{0, s.cluster, s.tpr, s.nv};
     }
-    return Plan{3, 1, 256, 0};
+    return Plan{3, 1, generic_tpr(a, es, res), 0};
 }
 
 template <typename T, bool RES>
@@ -227,7 +249,7 @@ int run(const RmsArgs& a, bool vector_ok, cudaStream_t st) {
             if (rc >= 0) return rc;
         }
     }
-    return launch_rms_generic<T, RES>(a, st);
+    return launch_rms_generic<T, RES>(a, generic_tpr(a, static_cast<int>(sizeof(T)), RES), st);
 }
 
 template <bool RES>
@@ -349,6 +371,15 @@ extern "C" int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int
         return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "rmsnorm launch shape (cluster %d, %d threads, %d vectors) is not built",
                          cluster, threads_per_row, vectors_per_thread);
     g_override = {cluster, threads_per_row, vectors_per_thread};
+    return AKO_B200_OK;
+}
+
+extern "C" int ako_b200_rmsnorm_set_generic(int threads_per_row) {
+    clear_error();
+    if (threads_per_row != 0 && threads_per_row != 32 && threads_per_row != kGenericThreads)
+        return set_error(AKO_B200_ERR_INVALID_ARGUMENT, "any-width rmsnorm takes 32 or %d threads per row, got %d",
+                         kGenericThreads, threads_per_row);
+    g_generic_tpr = threads_per_row;
     return AKO_B200_OK;
 }
 #endif  // AKO_B200_MEASUREMENT

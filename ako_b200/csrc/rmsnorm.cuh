@@ -302,14 +302,14 @@ __device__ __forceinline__ uint4 shifted16(const uint4* p) {
 // aligned blocks reach outside the weight tensor (only the first or last
 // can, when the weight itself is not 16-byte aligned at its ends) reads its
 // weights element by element, so every access stays inside the tensor.
-template <typename T, bool RES, int MIS>
+template <typename T, bool RES, int MIS, int TPR>
 __device__ __forceinline__ void generic_body_shifted(const RmsArgs& a, const T* xr, const T* ro, T* yr, int head,
-                                                     int nvec, float inv, const uint4* wv) {
+                                                     int nvec, float inv, const uint4* wv, int lane) {
     constexpr int VEC = 16 / sizeof(T);
     using P = Packed<T, VEC>;
     const uintptr_t w_begin = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t w_end = w_begin + static_cast<uintptr_t>(a.h) * sizeof(T);
-    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+    for (int v = lane; v < nvec; v += TPR) {
         const int col = head + v * VEC;
         const P xv = RES ? ld_cached<T, VEC>(ro + col) : ld_cached<T, VEC>(xr + col);
         const uintptr_t blk = reinterpret_cast<uintptr_t>(wv + v);
@@ -335,13 +335,25 @@ __device__ __forceinline__ void generic_body_shifted(const RmsArgs& a, const T* 
     }
 }
 
-template <typename T, bool RES>
-__global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsArgs a) {
+// TPR threads per row: 256 (one CTA per row), or 32 for narrow rows (a warp
+// per row, four rows per 128-thread CTA, shuffle-only reduction).
+template <int TPR>
+constexpr int generic_threads() {
+    return TPR == 32 ? 128 : TPR;
+}
+
+template <typename T, bool RES, int TPR>
+__global__ void __launch_bounds__(generic_threads<TPR>()) rms_generic_kernel(const RmsArgs a) {
     constexpr int VEC = 16 / sizeof(T);
+    constexpr int ROWS = generic_threads<TPR>() / TPR;
     using P = Packed<T, VEC>;
-    __shared__ float scratch[kGenericThreads / 32];
+    __shared__ float scratch[TPR / 32];
     pdl_enter();
-    const int64_t row = blockIdx.x;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * ROWS + threadIdx.x / TPR;
+    const int lane = static_cast<int>(threadIdx.x % TPR);
+    // A warp whose row is past the end leaves: with a warp per row the
+    // reduction is shuffles only, and one-row CTAs have no such warps.
+    if (ROWS > 1 && row >= a.rows) return;
     const T* xr = static_cast<const T*>(a.x) + row * a.sx;
     const T* rr = RES ? static_cast<const T*>(a.r) + row * a.sr : nullptr;
     T* ro = RES ? static_cast<T*>(a.ro) + row * a.sro : nullptr;
@@ -374,9 +386,9 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
         }
         acc += static_cast<double>(__fmul_rn(f, f));
     };
-    for (int col = threadIdx.x; col < head; col += kGenericThreads) first_pass(col);
-    for (int col = tail + threadIdx.x; col < a.h; col += kGenericThreads) first_pass(col);
-    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+    for (int col = lane; col < head; col += TPR) first_pass(col);
+    for (int col = tail + lane; col < a.h; col += TPR) first_pass(col);
+    for (int v = lane; v < nvec; v += TPR) {
         const int col = head + v * VEC;
         P xv = ld_stream<T, VEC>(xr + col);
         if constexpr (RES) {
@@ -398,7 +410,7 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
         }
         acc += static_cast<double>(tree_sum<VEC>(sq));
     }
-    const float total = block_sum<kGenericThreads>(static_cast<float>(acc), scratch);
+    const float total = block_sum<TPR>(static_cast<float>(acc), scratch);
     const float inv = rms_inv(total, a);
 
     // The residual pass reads back what this same thread stored above, with
@@ -407,8 +419,8 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
         const float f = RES ? to_f32(ro[col]) : to_f32(xr[col]);
         yr[col] = from_f32<T>(__fmul_rn(__fmul_rn(f, inv), load_weight(a.w, a.wdtype, col)));
     };
-    for (int col = threadIdx.x; col < head; col += kGenericThreads) second_pass(col);
-    for (int col = tail + threadIdx.x; col < a.h; col += kGenericThreads) second_pass(col);
+    for (int col = lane; col < head; col += TPR) second_pass(col);
+    for (int col = tail + lane; col < a.h; col += TPR) second_pass(col);
     // The body's weights: with the row's dtype they are 16 contiguous bytes
     // per vector at a byte offset that is the same for every vector of the
     // row, so they come from two aligned 16-byte loads and a shift chosen
@@ -417,18 +429,18 @@ __global__ void __launch_bounds__(kGenericThreads) rms_generic_kernel(const RmsA
     if (a.wdtype == dtype_code<T>() && nvec > 0) {
         const uint4* wv = reinterpret_cast<const uint4*>(wb & ~uintptr_t{15});
         switch (static_cast<int>(wb & 15u)) {
-            case 0: generic_body_shifted<T, RES, 0>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 2: generic_body_shifted<T, RES, 2>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 4: generic_body_shifted<T, RES, 4>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 6: generic_body_shifted<T, RES, 6>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 8: generic_body_shifted<T, RES, 8>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 10: generic_body_shifted<T, RES, 10>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            case 12: generic_body_shifted<T, RES, 12>(a, xr, ro, yr, head, nvec, inv, wv); break;
-            default: generic_body_shifted<T, RES, 14>(a, xr, ro, yr, head, nvec, inv, wv); break;
+            case 0: generic_body_shifted<T, RES, 0, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 2: generic_body_shifted<T, RES, 2, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 4: generic_body_shifted<T, RES, 4, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 6: generic_body_shifted<T, RES, 6, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 8: generic_body_shifted<T, RES, 8, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 10: generic_body_shifted<T, RES, 10, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            case 12: generic_body_shifted<T, RES, 12, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
+            default: generic_body_shifted<T, RES, 14, TPR>(a, xr, ro, yr, head, nvec, inv, wv, lane); break;
         }
         return;
     }
-    for (int v = threadIdx.x; v < nvec; v += kGenericThreads) {
+    for (int v = lane; v < nvec; v += TPR) {
         const int col = head + v * VEC;
         const P xv = RES ? ld_cached<T, VEC>(ro + col) : ld_cached<T, VEC>(xr + col);
         P o;
@@ -555,9 +567,15 @@ int launch_rms_rows(const RmsArgs& a, int cluster, int tpr, int nv, cudaStream_t
 }
 
 template <typename T, bool RES>
-int launch_rms_generic(const RmsArgs& a, cudaStream_t st) {
-    return launch_ex(rms_generic_kernel<T, RES>, dim3(static_cast<unsigned>(a.rows)), dim3(kGenericThreads), 0, 1, st,
-                     a, RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)");
+int launch_rms_generic(const RmsArgs& a, int tpr, cudaStream_t st) {
+    const char* name = RES ? "rmsnorm_residual(generic)" : "rmsnorm(generic)";
+    if (tpr == 32) {
+        constexpr int rows = generic_threads<32>() / 32;
+        return launch_rows_kernel(rms_generic_kernel<T, RES, 32>, (a.rows + rows - 1) / rows, generic_threads<32>(), 1,
+                                  a, st, name);
+    }
+    return launch_ex(rms_generic_kernel<T, RES, kGenericThreads>, dim3(static_cast<unsigned>(a.rows)),
+                     dim3(kGenericThreads), 0, 1, st, a, name);
 }
 
 // Polls of a persistent kernel's bounded wait for a bulk copy (about a
@@ -583,8 +601,8 @@ int rms_chunks_for(int h, int es);
 #define AKO_RMS_DECLARE(T, KW)                                                        \
     KW template int launch_rms_rows<T, false>(const RmsArgs&, int, int, int, cudaStream_t); \
     KW template int launch_rms_rows<T, true>(const RmsArgs&, int, int, int, cudaStream_t);  \
-    KW template int launch_rms_generic<T, false>(const RmsArgs&, cudaStream_t);        \
-    KW template int launch_rms_generic<T, true>(const RmsArgs&, cudaStream_t);
+    KW template int launch_rms_generic<T, false>(const RmsArgs&, int, cudaStream_t);        \
+    KW template int launch_rms_generic<T, true>(const RmsArgs&, int, cudaStream_t);
 
 #ifndef AKO_RMS_INSTANTIATING
 AKO_RMS_DECLARE(float, extern)

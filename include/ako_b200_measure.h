@@ -43,6 +43,13 @@ int ako_b200_rmsnorm_set_launch(int cluster, int threads_per_row, int vectors_pe
 int ako_b200_rmsnorm_set_staging(int mode, int stages, int ctas_per_sm);
 
 /*
+ * RMSNorm any-width kernel (rows that are not whole 16-byte vectors, or
+ * pointers that are not 16-byte aligned): 32 threads per row (a warp per
+ * row) or 256 (a CTA per row); 0 restores the built-in choice by row width.
+ */
+int ako_b200_rmsnorm_set_generic(int threads_per_row);
+
+/*
  * Polls of the persistent kernels' bounded wait for a bulk copy (built-in:
  * 2^24, about a second). 0 makes every such wait run out at once, which
  * exercises the expiry path of ako_b200_take_device_status without any copy

@@ -147,6 +147,42 @@ def test_rmsnorm_generic_weight_alignments(cuda_device, dtype: str) -> None:
             assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", f"h={h} weight offset {off}")
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rmsnorm_generic_warp_and_cta_per_row(cuda_device, dtype: str) -> None:
+    """The any-width kernel with a warp per row (four rows per CTA, so row
+    counts that leave the last CTA part-empty) and with a CTA per row, forced
+    through the measurement build: ragged widths, rows starting off 16-byte
+    boundaries (a column slice of a wider tensor), fused and plain, a weight
+    of the row's dtype and an fp32 one, against the oracle."""
+    rng = np.random.default_rng(43)
+    with _native.measurement() as lib:
+        try:
+            for tpr in (32, 256):
+                assert lib.ako_b200_rmsnorm_set_generic(tpr) == 0
+                for h in (1, 7, 37, 1001, 2047, 4100):
+                    for rows, shift in ((1, 0), (5, 0), (9, 1), (6, 3)):
+                        xb = normal(rng, (rows, h + shift), 0, 1, dtype)
+                        rb = normal(rng, (rows, h + shift), 0, 1, dtype)
+                        x, r = xb[:, shift:], rb[:, shift:]
+                        w = normal(rng, (h,), 1, 0.1, dtype)
+                        w32 = normal(rng, (h,), 1, 0.1, O.F32)
+                        xt = to_torch(xb, dtype, cuda_device)[:, shift:]
+                        rt = to_torch(rb, dtype, cuda_device)[:, shift:]
+                        wt = to_torch(w, dtype, cuda_device)
+                        what = f"{tpr} threads/row h={h} rows={rows} shift={shift}"
+                        y = kernels.rmsnorm_cuda_sm100(xt, wt, 1e-6)
+                        assert_parity(C.rmsnorm(x, w, 1e-6, dtype), to_numpy(y), dtype, "rmsnorm", what)
+                        y, ro = kernels.rmsnorm_residual_cuda_sm100(xt, rt, wt, 1e-5)
+                        y_ref, ro_ref = C.rmsnorm_residual(x, r, w, 1e-5, dtype)
+                        np.testing.assert_array_equal(to_numpy(ro), ro_ref)
+                        assert_parity(y_ref, to_numpy(y), dtype, "rmsnorm_residual", what)
+                        y = kernels.rmsnorm_cuda_sm100(xt, to_torch(w32, O.F32, cuda_device), 1e-6)
+                        assert_parity(C.rmsnorm(x, w32, 1e-6, dtype, O.F32), to_numpy(y), dtype, "rmsnorm",
+                                      what + " fp32 weight")
+        finally:
+            lib.ako_b200_rmsnorm_set_generic(0)
+
+
 @pytest.mark.parametrize("dtype", (O.F16, O.BF16))
 def test_rmsnorm_fp32_weight(cuda_device, dtype: str) -> None:
     rng = np.random.default_rng(11)

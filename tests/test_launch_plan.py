@@ -39,7 +39,8 @@ def _built_in_choice():
     m = _native.measure_lib()
     for f in (lambda: m.ako_b200_rmsnorm_set_launch(0, 0, 0), lambda: m.ako_b200_rmsnorm_set_staging(0, 0, 0),
               lambda: m.ako_b200_swiglu_set_launch(0, 0), lambda: m.ako_b200_rope_set_launch(0),
-              lambda: m.ako_b200_swiglu_set_grid(0), lambda: m.ako_b200_swiglu_set_smem(0)):
+              lambda: m.ako_b200_swiglu_set_grid(0), lambda: m.ako_b200_swiglu_set_smem(0),
+              lambda: m.ako_b200_rmsnorm_set_generic(0)):
         f()
     yield
     m.ako_b200_rmsnorm_set_launch(0, 0, 0)
@@ -47,6 +48,7 @@ def _built_in_choice():
     m.ako_b200_swiglu_set_launch(0, 0)
     m.ako_b200_swiglu_set_grid(0)
     m.ako_b200_swiglu_set_smem(0)
+    m.ako_b200_rmsnorm_set_generic(0)
     m.ako_b200_rope_set_launch(0)
 
 
@@ -94,9 +96,23 @@ def test_built_in_choice(rows, h, dtype, residual, expected) -> None:
 
 
 def test_unaligned_and_ragged_calls_take_the_any_width_kernel() -> None:
-    assert plan(8192, 4096, BF16, True, aligned=False)[0] == GENERIC
-    assert plan(8192, 4100, BF16, False)[0] == GENERIC
+    assert plan(8192, 4096, BF16, True, aligned=False) == (GENERIC, 1, 256, 0)
+    assert plan(8192, 4100, BF16, True) == (GENERIC, 1, 256, 0)
     assert plan(8192, 4100, F32, False)[0] == ROWS  # 16400-byte fp32 rows are whole vectors
+    # narrow rows take a warp each (plain up to 8704 bytes, fused up to 6144), whatever the row count
+    for rows in (1, 7, 65536):
+        assert plan(rows, 1001, BF16, False) == (GENERIC, 1, 32, 0)
+        assert plan(rows, 3072, BF16, True, aligned=False) == (GENERIC, 1, 32, 0)
+        assert plan(rows, 3073, BF16, True, aligned=False) == (GENERIC, 1, 256, 0)
+        assert plan(rows, 4100, BF16, False) == (GENERIC, 1, 32, 0)
+        assert plan(rows, 2177, F32, False) == (GENERIC, 1, 256, 0)
+        assert plan(rows, 1023, F32, True) == (GENERIC, 1, 32, 0)
+    assert plan(8, 1537, F32, True) == (GENERIC, 1, 256, 0)
+    m = _native.measure_lib()
+    assert m.ako_b200_rmsnorm_set_generic(256) == 0
+    assert plan(8, 1001, BF16, False, lib=m) == (GENERIC, 1, 256, 0)
+    assert m.ako_b200_rmsnorm_set_generic(64) == 1 and m.ako_b200_rmsnorm_set_generic(0) == 0
+    assert plan(8, 1001, BF16, False, lib=m) == (GENERIC, 1, 32, 0)
 
 
 def test_measurement_overrides_are_followed() -> None:
