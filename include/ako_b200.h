@@ -189,7 +189,8 @@ int ako_b200_swiglu(const void* gate, int64_t gate_row_stride,
  * row-resident kernel (a thread-block cluster of *cluster CTAs, each row
  * slice held by *threads_per_row threads with *vectors_per_thread 16-byte
  * vectors), 1 for the staged and 2 for the chunked persistent kernel
- * (threads and vectors per thread; cluster 1), 3 for the any-width kernel.
+ * (threads and vectors per thread; cluster 1), 3 for the any-width kernel
+ * (*threads_per_row 32, a warp per row, or 256, a CTA per row).
  * `residual` selects the fused form; `aligned` says whether the call's
  * pointers and row strides are 16-byte aligned. Follows the library's
  * built-in choice (in the measurement build, any override in force). Not
