@@ -5,6 +5,7 @@
 * :func:`ako_b200.register` — adds them to AKO's dispatcher (drop-in).
 * :mod:`ako_b200.api` — AKO's public op API on the package's own dispatcher.
 * :mod:`ako_b200.host` — host-buffer entry points (PCIe-pipelined).
+* :mod:`ako_b200.bandwidth` — GB/s columns for AKO's benchmark reports.
 """
 
 from ako_b200.api import build_rope_tables, rmsnorm, rmsnorm_residual, rope, rope_qk, swiglu
