@@ -61,6 +61,13 @@ def _built_in_choice():
         (8192, 2048, BF16, True, (ROWS, 1, 128, 2)),
         (8192, 4096, F16, True, (ROWS, 1, 256, 2)),
         (8192, 8192, BF16, True, (ROWS, 1, 512, 2)),
+        # a few hundred fused rows: two vectors per thread
+        (512, 2048, BF16, True, (ROWS, 1, 128, 2)),
+        (256, 2048, BF16, True, (ROWS, 1, 256, 1)),
+        (256, 4096, F16, True, (ROWS, 1, 256, 2)),
+        (512, 4096, BF16, True, (ROWS, 1, 256, 2)),
+        (128, 4096, BF16, True, (ROWS, 1, 512, 1)),
+        (512, 4096, BF16, False, (ROWS, 1, 256, 2)),
         # decode: latency shapes and clusters
         (1, 4096, BF16, True, (ROWS, 1, 512, 1)),
         (1, 16384, BF16, True, (ROWS, 4, 512, 1)),
