@@ -8,6 +8,7 @@
 * :mod:`ako_b200.bandwidth` — GB/s columns for AKO's benchmark reports.
 """
 
+from ako_b200 import bandwidth
 from ako_b200.api import build_rope_tables, rmsnorm, rmsnorm_residual, rope, rope_qk, swiglu
 from ako_b200.kernels import (
     rmsnorm_cuda_sm100,
@@ -22,6 +23,7 @@ __version__ = "0.1.0"
 
 __all__ = [
     "__version__",
+    "bandwidth",
     "build_rope_tables",
     "register",
     "rmsnorm",
