@@ -83,8 +83,9 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 // FLAT: all three operands are dense (row stride == hidden_dim), so vector
 // i sits at element i * VEC of each. Otherwise rows come from FastDiv
-// (NARROW, total < 2^32) or a 64-bit division.
-template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW, int THREADS>
+// (NARROW, total < 2^32) or a 64-bit division. NC: 16-byte loads through the
+// non-coherent path without L1 allocation.
+template <typename T, int VEC, int UNROLL, bool FLAT, bool NARROW, int THREADS, bool NC = false>
 __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
     pdl_enter();
     using P = Packed<T, VEC>;
@@ -118,7 +119,10 @@ __global__ void __launch_bounds__(THREADS) swiglu_kernel(const SwigluArgs a) {
                     uo = row * a.su + col;
                     yo[k] = row * a.sy + col;
                 }
-                if constexpr (VEC * sizeof(T) == 16) {
+                if constexpr (VEC * sizeof(T) == 16 && NC) {
+                    g[k] = ld_stream_no_l1<T, VEC>(gp + go);
+                    u[k] = ld_stream_no_l1<T, VEC>(up + uo);
+                } else if constexpr (VEC * sizeof(T) == 16) {
                     g[k] = ld_stream<T, VEC>(gp + go);
                     u[k] = ld_stream<T, VEC>(up + uo);
                 } else {
@@ -156,7 +160,7 @@ constexpr int kFourResidentSmem = 48 * 1024;
 // The grid strides over the vectors with at most `threads_per_sm` threads
 // per SM (CTAs of THREADS threads); with `four_resident`, at most four CTAs
 // of it are on an SM at once (the rest run as those finish).
-template <typename T, int VEC, int UNROLL, int THREADS>
+template <typename T, int VEC, int UNROLL, int THREADS, bool NC = false>
 int launch(SwigluArgs a, bool flat, int threads_per_sm, bool four_resident, cudaStream_t st) {
     const int64_t per_cta = static_cast<int64_t>(THREADS) * UNROLL;
     int64_t grid = (a.total + per_cta - 1) / per_cta;
@@ -166,13 +170,13 @@ int launch(SwigluArgs a, bool flat, int threads_per_sm, bool four_resident, cuda
     const dim3 g(static_cast<unsigned>(grid));
     const int smem = g_smem_bytes > 0 ? g_smem_bytes : four_resident ? kFourResidentSmem : 0;
     if (flat)
-        return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
+        return launch_ex(swiglu_kernel<T, VEC, UNROLL, true, true, THREADS, NC>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
     if (a.total <= static_cast<int64_t>(UINT_MAX)) {
         a.row_div = FastDiv::make(static_cast<uint32_t>(a.per_row));
-        return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, true, THREADS>, g, dim3(THREADS), smem, 1, st, a,
+        return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, true, THREADS, NC>, g, dim3(THREADS), smem, 1, st, a,
                          "swiglu");
     }
-    return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
+    return launch_ex(swiglu_kernel<T, VEC, UNROLL, false, false, THREADS, NC>, g, dim3(THREADS), smem, 1, st, a, "swiglu");
 }
 
 // Launch choice for a call: bytes per access (16, 4 for decode-sized
@@ -181,6 +185,7 @@ int launch(SwigluArgs a, bool flat, int threads_per_sm, bool four_resident, cuda
 struct SwigluPlan {
     int access_bytes, threads, unroll, threads_per_sm;
     bool four_resident;
+    bool no_l1;  // 16-byte loads through the non-coherent path, no L1 allocation
 };
 
 // Thread budget per SM of the grid-stride grid, built-in: a full SM of
@@ -195,7 +200,7 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // reciprocals. In CUDA graphs on B200 this is 0.1 us faster per call
         // for fp16 and fp32 rows of 5632-14336 at 1-2 rows and the same for
         // bf16; above 2^15 elements 16-byte accesses are as fast or faster.
-        return SwigluPlan{4, 128, 1, kThreadsPerSm, false};
+        return SwigluPlan{4, 128, 1, kThreadsPerSm, false, false};
     }
     if (vector_ok) {
         // 256-thread CTAs with one vector of each input per thread (32
@@ -217,15 +222,24 @@ SwigluPlan swiglu_plan(int64_t rows, int64_t h, int es, bool vector_ok, bool fla
         // (1024 threads per SM): 2-3% faster than a full SM of one-vector
         // threads (bf16 16384 x 14336 packed 224.9 -> 218.5 us), and level
         // with two passes of four.
+        //
+        // Up to 2^22 vectors (operands of up to 64 MB, the problem within about
+        // 1.5x the L2), loads that allocate nothing in L1 (ld.global.nc
+        // .L1::no_allocate) stream 1-4% faster on every such config-4 cell
+        // measured on B200 (2048 rows, F 5632..14336, bf16 and fp16, dense and
+        // packed; bf16 dense 2048 x 14336 30.1 -> 28.9 us); from 4096 rows on
+        // they cost 5-10%.
         const int64_t total = rows * (h * es / 16);
         const bool small = total < static_cast<int64_t>(sm_count()) * kThreads * 4;
         const bool huge = total >= (int64_t{1} << 24);
-        return SwigluPlan{16, g_threads > 0 ? g_threads : (small ? 128 : kThreads),
-                          g_unroll > 0 ? g_unroll : (huge ? 2 : 1),
+        const int threads = g_threads > 0 ? g_threads : (small ? 128 : kThreads);
+        const int unroll = g_unroll > 0 ? g_unroll : (huge ? 2 : 1);
+        return SwigluPlan{16, threads, unroll,
                           g_threads_per_sm > 0 ? g_threads_per_sm : (huge && !flat ? 1024 : kThreadsPerSm),
-                          huge && flat && g_threads == 0 && g_threads_per_sm == 0};
+                          huge && flat && g_threads == 0 && g_threads_per_sm == 0,
+                          !small && total <= (int64_t{1} << 22) && threads == kThreads && unroll == 1};
     }
-    return SwigluPlan{es, 256, 4, kThreadsPerSm, false};
+    return SwigluPlan{es, 256, 4, kThreadsPerSm, false, false};
 }
 
 template <typename T, int VEC>
@@ -237,7 +251,9 @@ int launch_vec(const SwigluArgs& a, bool flat, const SwigluPlan& p, cudaStream_t
         case 64 * 16 + 2: return launch<T, VEC, 2, 64>(a, flat, tps, four, st);
         case 128 * 16 + 1: return launch<T, VEC, 1, 128>(a, flat, tps, four, st);
         case 128 * 16 + 2: return launch<T, VEC, 2, 128>(a, flat, tps, four, st);
-        case 256 * 16 + 1: return launch<T, VEC, 1, 256>(a, flat, tps, four, st);
+        case 256 * 16 + 1:
+            return p.no_l1 ? launch<T, VEC, 1, 256, true>(a, flat, tps, four, st)
+                           : launch<T, VEC, 1, 256>(a, flat, tps, four, st);
         case 256 * 16 + 4: return launch<T, VEC, 4, 256>(a, flat, tps, four, st);
         default: return launch<T, VEC, 2, 256>(a, flat, tps, four, st);
     }
