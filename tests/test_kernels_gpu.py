@@ -424,7 +424,7 @@ def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
             assert (int(m.group(3)), int(m.group(1)), int(m.group(2))) == (cluster, tpr, nv), (rows, h, got[:300])
         del x
 
-    # SwiGLU: swiglu_kernel<T, VEC, UNROLL, FLAT, NARROW, THREADS>
+    # SwiGLU: swiglu_kernel<T, VEC, UNROLL, FLAT, NARROW, THREADS, NC>
     for rows, f, dt, packed in ((16384, 14336, torch.bfloat16, False), (16384, 14336, torch.bfloat16, True),
                                 (64, 14336, torch.float16, False), (1, 14336, torch.float16, False),
                                 (7, 100, torch.bfloat16, False)):
@@ -434,7 +434,8 @@ def test_launch_plan_matches_the_launched_kernel(cuda_device) -> None:
         both = torch.randn(rows, 2 * f, device=cuda_device).to(dt)
         g, u = (both[:, :f], both[:, f:]) if packed else (both[:, :f].contiguous(), both[:, f:].contiguous())
         got = _kernel_names(lambda: kernels.swiglu_cuda_sm100(g, u))
-        m = re.search(r"swiglu_kernel<[^,]+, (\d+), (\d+), (?:true|false|1|0), (?:true|false|1|0), (\d+)>", got)
+        m = re.search(r"swiglu_kernel<[^,]+, (\d+), (\d+), (?:true|false|1|0), (?:true|false|1|0), (\d+)"
+                      r"(?:, (?:true|false|1|0))?>", got)
         assert m is not None, got[:300]
         es = torch.tensor([], dtype=dt).element_size()
         assert (int(m.group(1)) * es, int(m.group(3)), int(m.group(2))) == (access, threads, unroll), (rows, f, got[:300])
