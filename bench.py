@@ -13,19 +13,20 @@ back-to-back steps need no flush).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Multi-GPU (torchrun, one process per GPU): the step's batch is one global
-batch whose rows are split into contiguous blocks by
-``ako_b200.sharding.shard_range`` (strong scaling; ``--scaling weak`` gives
-every rank a whole batch instead). Every rank generates only its own rows,
-from seeds that depend on the global row index, so the union of the shards is
-the one-GPU batch. No collective touches the data path: only a barrier, the
+batch whose rows (batch entries for the RoPE workloads) are split into
+contiguous blocks by ``ako_b200.sharding.shard_range`` (strong scaling;
+``--scaling weak`` gives every rank a whole batch instead). Every rank
+generates only its own rows, from seeds that depend on the global row index,
+so the union of the shards is the one-GPU batch. No collective touches the data path: only a barrier, the
 max of the per-rank device times and the AND of the per-rank parity checks.
 
 * ``value``: whole-job GB/s = the global batch's bytes / the slowest rank's
   time, inputs resident in HBM, CUDA events on the launching stream around
   exactly K steps.
 * ``weak`` (N > 1): the same with a whole batch per rank.
-* ``parity``: rows of every shard against the C model of the kernels' fixed
-  summation order (bit for bit) and the reference-order oracle (the gate).
+* ``parity``: rows of every shard against the C oracle: RMSNorm against the C
+  model of the kernels' fixed summation order (bit for bit) and the
+  reference-order oracle (the gate), RoPE bit for bit, SwiGLU within 2 ulp.
 * ``e2e``: the same metric through the host-buffer call
   (``ako_b200.host.rmsnorm_residual_host``): pinned host inputs copied in and
   results copied out inside the timed region, every step.
