@@ -599,7 +599,13 @@ def main() -> None:
                "api": "ako_b200.host.rmsnorm_residual_host (pinned host buffers, chunked H2D/kernel/D2H "
                       "on three streams, C-ABI ako_b200_rmsnorm_residual per chunk)",
                "gpu_launches": k * world * host.launches_per_call(n, h, wl.element_size)}
-        del xh, rh, yh, roh
+        # The host path splits the rows into chunks; RMSNorm's summation order
+        # does not depend on the row count, so its outputs must equal the
+        # device call's bit for bit.
+        y_dev, ro_dev = wl.fn()
+        same = bool(torch.equal(yh, y_dev.cpu()) and torch.equal(roh, ro_dev.cpu()))
+        e2e["outputs_equal_device_call"] = sharding.all_over_ranks(same, device)
+        del xh, rh, yh, roh, y_dev, ro_dev
 
     # Every rank has finished its GPU work with the same collective steps; the
     # legs below run on rank 0 alone at N = 1.
