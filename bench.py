@@ -24,9 +24,10 @@ max of the per-rank device times and the AND of the per-rank parity checks.
   time, inputs resident in HBM, CUDA events on the launching stream around
   exactly K steps.
 * ``weak`` (N > 1): the same with a whole batch per rank.
-* ``parity``: rows of every shard against the C oracle: RMSNorm against the C
-  model of the kernels' fixed summation order (bit for bit) and the
-  reference-order oracle (the gate), RoPE bit for bit, SwiGLU within 2 ulp.
+* ``parity``: every shard against the C oracle: for RMSNorm every row against
+  the C model of the kernels' fixed summation order (bit for bit) and three
+  rows against the reference-order oracle (the gate); three rows (batch
+  entries) of RoPE bit for bit and of SwiGLU within 2 ulp.
 * ``e2e``: the same metric through the host-buffer call
   (``ako_b200.host.rmsnorm_residual_host``): pinned host inputs copied in and
   results copied out inside the timed region, every step.
@@ -292,7 +293,7 @@ def ncu_traffic(workload: str) -> int | None:
 
 
 # ------------------------------------------------------------------ parity
-def shard_parity(wl: Workload) -> dict:
+def shard_parity(wl: Workload, threads: int | None = None) -> dict:
     """This rank's shard on the host against the C oracle: three of its rows
     (its first, middle and last; for RoPE, those batch entries). RMSNorm rows
     are held to the C model of the kernels' fixed summation order bit for bit
@@ -327,22 +328,32 @@ def shard_parity(wl: Workload) -> dict:
     xs, w = host(wl.x[sel]), host(wl.w)
     # rows of whole 16-byte vectors run on the vector kernels, held to the fixed-order model
     vectors = (xs.shape[-1] * xs.dtype.itemsize) % 16 == 0
+    full = None
     if wl.op == "rmsnorm_residual":
         rs = host(wl.r[sel])
-        y, ro = (host(t[sel]) for t in wl.fn())
+        y_dev, ro_dev = wl.fn()
+        y, ro = host(y_dev[sel]), host(ro_dev[sel])
         yo, roo = C.rmsnorm_residual(xs, rs, w, 1e-5, dt)
         ok = bool(np.array_equal(ro, roo))
         if vectors:
-            ym, rom = C.rmsnorm_fixed_order(xs, rs, w, 1e-5, dt)
-            ok = ok and bool(np.array_equal(y, ym) and np.array_equal(ro, rom))
+            # every row of the shard against the fixed-order model, bit for bit
+            ym, rom = C.rmsnorm_fixed_order(host(wl.x), host(wl.r), w, 1e-5, dt, threads=threads)
+            full = bool(np.array_equal(host(y_dev), ym) and np.array_equal(host(ro_dev), rom))
+            ok = ok and full
+        del y_dev, ro_dev
     else:
-        y = host(wl.fn()[sel])
+        y_dev = wl.fn()
+        y = host(y_dev[sel])
         yo = C.rmsnorm(xs, w, 1e-6, dt)
         if vectors:
-            ok = bool(np.array_equal(y, C.rmsnorm_fixed_order(xs, None, w, 1e-6, dt)))
+            full = bool(np.array_equal(host(y_dev), C.rmsnorm_fixed_order(host(wl.x), None, w, 1e-6, dt,
+                                                                          threads=threads)))
+            ok = full
+        del y_dev
     worst = int(O.ulp_distance(yo, y, dt).max())
     ok = ok and worst <= (2 if dt != O.F32 else 6)
-    return {"ok": ok, "rows": [wl.lo + i for i in sel], "max_ulp_vs_reference_order": worst}
+    return {"ok": ok, "rows": [wl.lo + i for i in sel], "max_ulp_vs_reference_order": worst,
+            "all_rows_bit_exact_vs_fixed_order_model": full, "rows_checked_bit_exact": n if full is not None else 0}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -563,7 +574,7 @@ def main() -> None:
     step_bytes = sharding.sum_over_ranks(wl.bytes, device)  # the global batch (strong) or N batches (weak)
     value = step_bytes / (per_step_ms * 1e-3) / 1e9
     achieved = wl.bytes / ((ms / args.steps) * 1e-3) / 1e9  # this rank's kernel
-    parity = shard_parity(wl)
+    parity = shard_parity(wl, threads=max(1, len(os.sched_getaffinity(0)) // world))
     parity_all = sharding.all_over_ranks(parity["ok"], device)
 
     weak = None
